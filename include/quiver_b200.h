@@ -1,0 +1,189 @@
+/*
+ * quiver_b200.h -- C ABI of the B200 engine for Quiver's query hot path.
+ *
+ * The engine replaces the reference's GPU search engine behind its own
+ * callers.  Every entry point names the reference interface it stands in
+ * for (path:line inside ruc-system/quiver-ae).  No C++ or torch types cross
+ * this boundary: plain pointers, sizes and an int status.
+ *
+ * Status: every function returns QV_OK (0) or a positive QV_ERR_* code and
+ * sets a thread-local message readable through qv_last_error().  Nothing
+ * throws across the ABI (the reference throws std::runtime_error from
+ * CHECK_CUDA, src/shared/common/cuda_utils.cuh:17-24, and calls
+ * std::exit(1) on bad configuration, src/quiver/search.cu:402-407; here both
+ * become return codes so the caller decides).
+ *
+ * Threading: an engine is thread-compatible -- one search at a time per
+ * engine, like run_persistent_search, which is called from one host thread.
+ * Different engines may be used from different threads.
+ */
+#ifndef QUIVER_B200_H
+#define QUIVER_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define QV_OK 0
+#define QV_ERR_INVALID_ARG 1  /* a parameter is out of its documented range */
+#define QV_ERR_IO 2           /* an index/query file cannot be read */
+#define QV_ERR_BAD_INDEX 3    /* index files are inconsistent or malformed */
+#define QV_ERR_CUDA 4         /* a CUDA runtime call failed */
+#define QV_ERR_DEVICE 5       /* the search kernel reported a fault in the data */
+#define QV_ERR_UNSUPPORTED 6  /* a configuration this build does not implement */
+#define QV_ERR_OOM 7          /* device or pinned host memory exhausted */
+
+/* Element type of base vectors (src/shared/common/data_type.hpp:5-9). */
+#define QV_UINT8 0
+#define QV_FLOAT 1
+#define QV_INT8 2
+
+/* Where the graph pages (vector + adjacency records) live. */
+#define QV_PAGES_HBM 0   /* device memory of the engine's GPU */
+#define QV_PAGES_HOST 1  /* pinned, mapped host DRAM read over PCIe */
+
+/* Early-exit policy (src/quiver/io_control.cuh:41-46; the CLI accepts only
+ * "none" and "gpruning", bin/quiver_search.cu:48-54). */
+#define QV_EXIT_NONE 0
+#define QV_EXIT_GPRUNING 2
+
+/* PQ lookup-table precision inside the search kernel. */
+#define QV_LUT_FP32 0  /* fp32 table, bit-identical ADC sums to the reference */
+
+typedef struct qv_engine qv_engine;
+
+/* Index layout, the fields of shared::Layout (src/shared/common/layout.hpp:7-19)
+ * as parse_diskann_metadata fills them (bin/common/metadata.hpp:15-72). */
+typedef struct {
+  int64_t num_points;
+  int64_t dim;
+  int64_t max_degree;      /* max_m0 = R */
+  int64_t node_size;       /* max_node_len */
+  int64_t data_size;       /* dim * element size */
+  int64_t nodes_per_page;
+  int64_t num_pages;
+  int64_t medoid;          /* enter_point */
+  int32_t data_type;       /* QV_UINT8 / QV_FLOAT / QV_INT8 */
+  int32_t num_chunks;      /* PQ subspaces M */
+} qv_index_info;
+
+/* Engine creation from an index directory.  Replaces
+ * bin_common::prepare_search_setup (bin/common/search_setup.hpp:73-119) +
+ * shared::create_mem_loader_sync (src/shared/io/loader.hpp:43-45) +
+ * shared::PQSearch::read_data / init_device (src/shared/index/pq_search.cu:62-177). */
+typedef struct {
+  const char* index_dir;          /* holds *_disk.index and *_pq_pivots.bin / *_pq_compressed.bin */
+  int32_t data_type;              /* QV_UINT8 / QV_FLOAT / QV_INT8 */
+  const char* memory_backend;     /* "heap" or "mmap": how the page file is read (memory_backend.hpp:7-20) */
+  const char* memory_index_file;  /* NULL or "" -> the discovered *_disk.index */
+  int32_t device;                 /* CUDA ordinal */
+  int32_t page_store;             /* QV_PAGES_HBM or QV_PAGES_HOST */
+  int32_t validate;               /* 1: check every adjacency list at load (degree <= R, ids < N) */
+} qv_engine_opts;
+
+/* Index arrays already in host memory, in the on-disk layouts:
+ * pages = the *_disk.index file without its 4 KB header page
+ * (src/shared/io/mem_loader.cpp:28-44), pivots = [256 x dim] fp32 as stored
+ * in *_pq_pivots.bin, chunk_offsets = [M+1], codes = [N x M]. */
+typedef struct {
+  qv_index_info info;
+  const uint8_t* pages;
+  const uint8_t* codes;
+  const float* pivots;
+  const float* centroid;
+  const int32_t* chunk_offsets;
+} qv_index_arrays;
+
+/* Search knobs.  Mirrors the arguments of quiver::run_persistent_search
+ * (src/quiver/search.cuh:45-66) and the CLI defaults
+ * (bin/common/cli_shared.hpp:14-25, bin/quiver_search.cu:67-79, 202-205). */
+typedef struct {
+  int32_t topk;                   /* default 10 */
+  int32_t ef_search;              /* default 30 */
+  int32_t pipe_width;             /* W lanes per query, 1..16 (cli_validation.hpp:9) */
+  int32_t queries_per_block;      /* query slots (warps) per CTA, 1..8; 0 = auto */
+  int32_t num_blocks;             /* persistent CTAs; 0 = one wave on every SM */
+  int32_t early_exit_policy;      /* QV_EXIT_NONE / QV_EXIT_GPRUNING */
+  int32_t gpruning_warmup_steps;  /* default 10 */
+  int32_t gpruning_patience;      /* default 8 */
+  int32_t lut_mode;               /* QV_LUT_FP32 */
+} qv_search_opts;
+
+typedef struct {
+  double h2d_ms;                  /* queries host -> device */
+  double kernel_ms;               /* search kernel (CUDA events) */
+  double d2h_ms;                  /* results device -> host */
+  double total_ms;                /* whole call */
+  int64_t expansions;             /* node records fetched (sum of per-query steps) */
+  int64_t neighbors_scored;       /* PQ codes gathered (sum of degrees) */
+  int32_t grid;                   /* CTAs launched */
+  int32_t slots_per_block;        /* query slots (warps) per CTA */
+  int32_t smem_per_block;         /* dynamic shared memory bytes per CTA */
+  int32_t blocks_per_sm;          /* resident CTAs per SM */
+} qv_search_stats;
+
+const char* qv_version(void);
+const char* qv_last_error(void);
+void qv_search_opts_default(qv_search_opts* opts);
+
+int qv_engine_create(const qv_engine_opts* opts, qv_engine** out);
+int qv_engine_create_from_arrays(const qv_index_arrays* arrays, int32_t device,
+                                 int32_t page_store, qv_engine** out);
+int qv_engine_info(const qv_engine* engine, qv_index_info* info);
+void qv_engine_destroy(qv_engine* engine);
+
+/* Search with HOST buffers: queries [nq x dim] fp32 (the reference's float
+ * query array, bin/common/data_io.hpp:73-108), ids/dists [nq x topk] and
+ * found [nq].  Unfilled result slots hold id -1 and distance +inf, as the
+ * reference initialises them (kernel_q1.cuh:192-195).  Replaces
+ * quiver::run_persistent_search (src/quiver/search.cuh:45-66).  `found` and
+ * `stats` may be NULL. */
+int qv_search(qv_engine* engine, const float* queries, int64_t nq, int64_t dim,
+              const qv_search_opts* opts, int32_t* ids, float* dists,
+              int32_t* found, qv_search_stats* stats);
+
+/* qv_search plus the per-query service latency: query_ms[i] is the time
+ * (ms, GPU global timer) from the moment a query slot took query i to the
+ * moment its results were written.  The reference's QueryLatency(ms) runs
+ * from host admission to host completion (src/quiver/search.cu:1007-1044);
+ * with every query admitted at the call, the host view of query i is its
+ * queueing delay plus this service time. */
+int qv_search_timed(qv_engine* engine, const float* queries, int64_t nq, int64_t dim,
+                    const qv_search_opts* opts, int32_t* ids, float* dists,
+                    int32_t* found, float* query_ms, qv_search_stats* stats);
+
+/* Same search with DEVICE buffers on the engine's GPU, enqueued on `stream`
+ * (a cudaStream_t; NULL = the engine's own stream) without a host
+ * synchronisation.  steps [nq] (expansions) and nbrs [nq] (PQ codes
+ * gathered) may be NULL.  Errors the kernel detects in the data are
+ * reported by qv_check_device_status after the stream has drained. */
+int qv_search_device(qv_engine* engine, const float* d_queries, int64_t nq,
+                     const qv_search_opts* opts, int32_t* d_ids, float* d_dists,
+                     int32_t* d_found, int32_t* d_steps, int64_t* d_nbrs,
+                     void* stream);
+int qv_check_device_status(qv_engine* engine);
+
+/* Launch geometry qv_search_device would use (grid, slots, smem). */
+int qv_plan(qv_engine* engine, const qv_search_opts* opts, int64_t nq,
+            qv_search_stats* plan);
+
+/* Component kernels on device buffers, for testing the stages in isolation.
+ *   qv_build_lut_device: LUT [nq x M x 256] and q'' [nq x dim]
+ *       (PQSearchData::init_query, src/shared/index/pq_device.cuh:9-36)
+ *   qv_adc_device: dist[i] = sum_j LUT[q(i)][j][code(id[i])[j]] for pairs
+ *       (query_of[i], ids[i]) (kernel_helpers.cuh:271-286)
+ *   qv_exact_l2_device: square_sum_32 of q''[query_of[i]] against node ids[i]
+ *       read from the page store (gpu_primitives.cuh:26-44) */
+int qv_build_lut_device(qv_engine* engine, const float* d_queries, int64_t nq,
+                        float* d_lut, float* d_q2, void* stream);
+int qv_adc_device(qv_engine* engine, const float* d_lut, const int32_t* d_query_of,
+                  const int32_t* d_ids, int64_t n, float* d_out, void* stream);
+int qv_exact_l2_device(qv_engine* engine, const float* d_q2, const int32_t* d_query_of,
+                       const int32_t* d_ids, int64_t n, float* d_out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* QUIVER_B200_H */

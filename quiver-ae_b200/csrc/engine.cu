@@ -1,0 +1,660 @@
+// engine.cu -- host runtime and C ABI of the B200 search engine.
+//
+// Owns the device copies of one index (page store, PQ codes, transposed
+// pivots, centroid, chunk offsets), plans the launch geometry of the
+// persistent search kernel from its shared-memory footprint, and runs
+// searches with host or device buffers.  Replaces the reference's
+// quiver::run_persistent_search (src/quiver/search.cu:357-1361): there is
+// no CPU poll thread and no host-mapped IO protocol, because node records
+// are read by the kernel directly from HBM (or from mapped host DRAM).
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <chrono>
+#include <cstdio>
+#include <cstring>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "index_io.h"
+#include "quiver_b200.h"
+#include "plan.h"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+struct CudaError : qv::IoError {
+  explicit CudaError(const std::string& m) : qv::IoError(QV_ERR_CUDA, m) {}
+};
+
+void check_cuda(cudaError_t e, const char* what, int line) {
+  if (e == cudaSuccess) return;
+  const int code = (e == cudaErrorMemoryAllocation) ? QV_ERR_OOM : QV_ERR_CUDA;
+  throw qv::IoError(code, std::string(what) + " failed: " + cudaGetErrorString(e) +
+                              " (engine.cu:" + std::to_string(line) + ")");
+}
+#define CK(call) check_cuda((call), #call, __LINE__)
+
+template <class F>
+int guarded(F&& f) {
+  try {
+    f();
+    return QV_OK;
+  } catch (const qv::IoError& e) {
+    g_last_error = e.what();
+    return e.code;
+  } catch (const std::bad_alloc&) {
+    g_last_error = "host allocation failed";
+    return QV_ERR_OOM;
+  } catch (const std::exception& e) {
+    g_last_error = e.what();
+    return QV_ERR_INVALID_ARG;
+  }
+}
+
+[[noreturn]] void fail(int code, const std::string& m) { throw qv::IoError(code, m); }
+
+int64_t round_up(int64_t v, int64_t a) { return (v + a - 1) / a * a; }
+
+}  // namespace
+
+struct qv_engine {
+  int device = 0;
+  qv::Layout L;
+  int32_t M = 0;
+  bool pages_host = false;
+  uint8_t* d_pages = nullptr;   // what the kernel dereferences
+  uint8_t* h_pages = nullptr;   // pinned mapped host allocation (host store)
+  uint8_t* d_codes = nullptr;
+  float* d_pivots_t = nullptr;
+  float* d_centroid = nullptr;
+  int32_t* d_chunk_off = nullptr;
+  int32_t* d_scratch = nullptr;  // [0] work counter, [1..4] error info
+  int num_sms = 0;
+  int max_smem_optin = 0;
+  cudaStream_t stream = nullptr;
+  cudaEvent_t ev[4] = {nullptr, nullptr, nullptr, nullptr};
+  // staging for host-buffer searches
+  float* d_q = nullptr;
+  int32_t* d_ids = nullptr;
+  float* d_dists = nullptr;
+  int32_t* d_found = nullptr;
+  int32_t* d_steps = nullptr;
+  int64_t* d_nbrs = nullptr;
+  int64_t* d_time = nullptr;
+  int64_t cap_q = 0, cap_r = 0, cap_n = 0;
+
+  ~qv_engine() {
+    if (device >= 0) cudaSetDevice(device);
+    for (auto* p : {(void*)d_codes, (void*)d_pivots_t, (void*)d_centroid, (void*)d_chunk_off,
+                    (void*)d_scratch, (void*)d_q, (void*)d_ids, (void*)d_dists, (void*)d_found,
+                    (void*)d_steps, (void*)d_nbrs, (void*)d_time})
+      if (p) cudaFree(p);
+    if (pages_host) {
+      if (h_pages) cudaFreeHost(h_pages);
+    } else if (d_pages) {
+      cudaFree(d_pages);
+    }
+    for (auto& e : ev)
+      if (e) cudaEventDestroy(e);
+    if (stream) cudaStreamDestroy(stream);
+  }
+};
+
+namespace {
+
+// ------------------------------------------------------------ planning --
+
+using qv::Plan;
+
+void validate_opts(const qv_engine* e, const qv_search_opts& o) {
+  if (o.topk < 1 || o.topk > 1024) fail(QV_ERR_INVALID_ARG, "topk must be in [1, 1024]");
+  if (o.ef_search < 1 || o.ef_search > 4096) fail(QV_ERR_INVALID_ARG, "ef_search must be in [1, 4096]");
+  if (o.pipe_width < 1 || o.pipe_width > qvk::kMaxPipeWidth)
+    fail(QV_ERR_INVALID_ARG, "--pipe-width must be in [1, 16]");
+  if (o.queries_per_block < 0 || o.queries_per_block > 8)
+    fail(QV_ERR_INVALID_ARG, "--queries-per-block must be in [1, 8]");
+  if (o.num_blocks < 0) fail(QV_ERR_INVALID_ARG, "--num-blocks must be positive");
+  if (o.early_exit_policy != QV_EXIT_NONE && o.early_exit_policy != QV_EXIT_GPRUNING)
+    fail(QV_ERR_INVALID_ARG, "early-exit policy must be none or gpruning");
+  if (o.lut_mode != QV_LUT_FP32) fail(QV_ERR_UNSUPPORTED, "only the fp32 LUT mode is built");
+  (void)e;
+}
+
+Plan make_plan(qv_engine* e, const qv_search_opts& o, int64_t nq) {
+  validate_opts(e, o);
+  Plan pl;
+  const auto& L = e->L;
+  pl.smax = L.max_degree <= 64 ? 2 : 4;
+  pl.mc = e->M == 32 ? 32 : 0;
+  const int G = pl.smax <= 2 ? 4 : 2;
+  int64_t off = 0;
+  auto take = [&](int64_t bytes) {
+    off = round_up(off, 16);
+    const int64_t r = off;
+    off += bytes;
+    return static_cast<int32_t>(r);
+  };
+  auto& y = pl.lay;
+  y.off_lut = take(int64_t(e->M) * qvk::kPivots * 4);
+  y.off_q2 = take(L.dim * 4);
+  y.off_lid = take(int64_t(o.ef_search) * 4);
+  y.off_ldist = take(int64_t(o.ef_search) * 4);
+  y.off_nid = take(32 * pl.smax * 4);
+  y.off_ndist = take(32 * pl.smax * 4);
+  y.off_mid = take((int64_t(o.ef_search) + 32 * pl.smax) * 4);
+  y.off_mdist = take((int64_t(o.ef_search) + 32 * pl.smax) * 4);
+  y.off_rid = take(int64_t(o.topk) * 4);
+  y.off_rdist = take(int64_t(o.topk) * 4);
+  y.rec_stride = static_cast<int32_t>(round_up(L.data_size, 16));
+  y.off_rec = take(int64_t(G) * y.rec_stride);
+  y.off_lane = take(qvk::kMaxPipeWidth * 4);
+  y.bytes = static_cast<int32_t>(round_up(off, 16));
+  if (y.bytes > e->max_smem_optin)
+    fail(QV_ERR_UNSUPPORTED, "one query slot needs " + std::to_string(y.bytes) +
+                                 " B of shared memory, above the per-CTA limit");
+
+  switch (L.data_type) {
+    case QV_UINT8: qv::bind_search_u8(pl); break;
+    case QV_INT8: qv::bind_search_i8(pl); break;
+    default: qv::bind_search_f32(pl); break;
+  }
+  CK(cudaFuncSetAttribute(pl.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, e->max_smem_optin));
+
+  auto occupancy = [&](int slots) {
+    int occ = 0;
+    const int smem = slots * y.bytes;
+    if (smem > e->max_smem_optin) return 0;
+    CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, pl.fn, slots * 32, smem));
+    return occ;
+  };
+  if (o.queries_per_block > 0) {
+    pl.slots = o.queries_per_block;
+    pl.blocks_per_sm = occupancy(pl.slots);
+    if (pl.blocks_per_sm == 0)
+      fail(QV_ERR_UNSUPPORTED, std::to_string(pl.slots) + " query slots of " + std::to_string(y.bytes) +
+                                   " B do not fit in one CTA");
+  } else {
+    int best = 0;
+    for (int slots = 1; slots <= 8; ++slots) {
+      const int occ = occupancy(slots);
+      if (occ * slots >= best && occ > 0) {
+        best = occ * slots;
+        pl.slots = slots;
+        pl.blocks_per_sm = occ;
+      }
+    }
+    if (best == 0) fail(QV_ERR_UNSUPPORTED, "a query slot does not fit in shared memory");
+  }
+  pl.smem = pl.slots * y.bytes;
+  const int64_t wave = int64_t(pl.blocks_per_sm) * e->num_sms;
+  int64_t grid = o.num_blocks > 0 ? std::min<int64_t>(o.num_blocks, wave) : wave;
+  const int64_t needed = (nq + pl.slots - 1) / pl.slots;
+  grid = std::max<int64_t>(1, std::min(grid, needed));
+  pl.grid = static_cast<int>(grid);
+  return pl;
+}
+
+qvk::SearchParams make_params(const qv_engine* e, const Plan& pl, const qv_search_opts& o,
+                              const float* d_q, int64_t nq, int32_t* ids, float* dists,
+                              int32_t* found, int32_t* steps, int64_t* nbrs, int64_t* times = nullptr) {
+  qvk::SearchParams p{};
+  p.pages = e->d_pages;
+  p.codes = e->d_codes;
+  p.pivots_t = e->d_pivots_t;
+  p.centroid = e->d_centroid;
+  p.chunk_off = e->d_chunk_off;
+  p.queries = d_q;
+  p.out_ids = ids;
+  p.out_dists = dists;
+  p.out_found = found;
+  p.out_steps = steps;
+  p.out_nbrs = nbrs;
+  p.out_time = times;
+  p.work_counter = e->d_scratch;
+  p.error_info = e->d_scratch + 1;
+  p.num_points = e->L.num_points;
+  p.nq = nq;
+  // Each pipe iteration expands at least one unvisited node and a node is
+  // expanded at most twice (the entry, once from the boot and once from the
+  // list), so N + W + 8 iterations bound every legal walk.
+  p.max_iters = e->L.num_points + o.pipe_width + 8;
+  p.dim = static_cast<int32_t>(e->L.dim);
+  p.M = e->M;
+  p.R = static_cast<int32_t>(e->L.max_degree);
+  p.node_size = static_cast<int32_t>(e->L.node_size);
+  p.data_words = static_cast<int32_t>(e->L.data_size / 4);
+  p.npp = static_cast<int32_t>(e->L.nodes_per_page);
+  p.ef = o.ef_search;
+  p.k = o.topk;
+  p.W = o.pipe_width;
+  p.early_policy = o.early_exit_policy;
+  p.gp_warmup = o.gpruning_warmup_steps;
+  p.gp_patience = o.gpruning_patience;
+  p.medoid = static_cast<int32_t>(e->L.medoid);
+  p.lay = pl.lay;
+  return p;
+}
+
+void enqueue_search(qv_engine* e, const Plan& pl, const qvk::SearchParams& p, cudaStream_t st) {
+  CK(cudaMemsetAsync(e->d_scratch, 0, 8 * sizeof(int32_t), st));
+  pl.launch(p, pl.grid, pl.slots * 32, pl.smem, st);
+  CK(cudaGetLastError());
+}
+
+void read_device_status(qv_engine* e) {
+  int32_t info[4];
+  CK(cudaMemcpy(info, e->d_scratch + 1, sizeof(info), cudaMemcpyDeviceToHost));
+  if (info[0] == qvk::kErrNone) return;
+  const char* what = info[0] == qvk::kErrNeighborRange ? "a neighbour id >= num_points"
+                   : info[0] == qvk::kErrDegree        ? "a stored degree above R"
+                   : info[0] == qvk::kErrHopCap        ? "a walk beyond its iteration bound"
+                                                       : "an unknown device error";
+  fail(QV_ERR_DEVICE, std::string("search kernel found ") + what + " (query " +
+                          std::to_string(info[1]) + ", node/step " + std::to_string(info[2]) + ")");
+}
+
+// ------------------------------------------------------ engine set-up --
+
+void init_device_side(qv_engine* e, int device) {
+  e->device = device;
+  int count = 0;
+  CK(cudaGetDeviceCount(&count));
+  if (device < 0 || device >= count) fail(QV_ERR_INVALID_ARG, "CUDA device ordinal out of range");
+  CK(cudaSetDevice(device));
+  CK(cudaDeviceGetAttribute(&e->num_sms, cudaDevAttrMultiProcessorCount, device));
+  CK(cudaDeviceGetAttribute(&e->max_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device));
+  CK(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking));
+  for (auto& ev : e->ev) CK(cudaEventCreate(&ev));
+  CK(cudaMalloc(&e->d_scratch, 8 * sizeof(int32_t)));
+  CK(cudaMemset(e->d_scratch, 0, 8 * sizeof(int32_t)));
+}
+
+void upload_pq(qv_engine* e, const float* pivots, const float* centroid, const int32_t* chunk_off,
+               const uint8_t* codes) {
+  const int64_t dim = e->L.dim;
+  std::vector<float> pt(static_cast<size_t>(dim) * qvk::kPivots);
+  for (int j = 0; j < qvk::kPivots; ++j)
+    for (int64_t i = 0; i < dim; ++i) pt[i * qvk::kPivots + j] = pivots[j * dim + i];
+  CK(cudaMalloc(&e->d_pivots_t, pt.size() * 4));
+  CK(cudaMemcpy(e->d_pivots_t, pt.data(), pt.size() * 4, cudaMemcpyHostToDevice));
+  CK(cudaMalloc(&e->d_centroid, dim * 4));
+  CK(cudaMemcpy(e->d_centroid, centroid, dim * 4, cudaMemcpyHostToDevice));
+  CK(cudaMalloc(&e->d_chunk_off, (e->M + 1) * 4));
+  CK(cudaMemcpy(e->d_chunk_off, chunk_off, (e->M + 1) * 4, cudaMemcpyHostToDevice));
+  const size_t cb = static_cast<size_t>(e->L.num_points) * e->M;
+  // +16 so 16-byte code loads of the last point stay inside the allocation
+  CK(cudaMalloc(&e->d_codes, cb + 16));
+  CK(cudaMemcpy(e->d_codes, codes, cb, cudaMemcpyHostToDevice));
+}
+
+void alloc_pages(qv_engine* e, int32_t page_store) {
+  const size_t bytes = static_cast<size_t>(e->L.num_pages) * qv::kPage;
+  if (page_store == QV_PAGES_HOST) {
+    e->pages_host = true;
+    CK(cudaHostAlloc(&e->h_pages, bytes, cudaHostAllocMapped | cudaHostAllocPortable));
+    CK(cudaHostGetDevicePointer(reinterpret_cast<void**>(&e->d_pages), e->h_pages, 0));
+  } else if (page_store == QV_PAGES_HBM) {
+    CK(cudaMalloc(&e->d_pages, bytes));
+  } else {
+    fail(QV_ERR_INVALID_ARG, "page_store must be QV_PAGES_HBM or QV_PAGES_HOST");
+  }
+}
+
+void ensure_staging(qv_engine* e, int64_t nq, int64_t k) {
+  const int64_t q = nq * e->L.dim, r = nq * k;
+  if (q > e->cap_q) {
+    if (e->d_q) CK(cudaFree(e->d_q));
+    CK(cudaMalloc(&e->d_q, q * 4));
+    e->cap_q = q;
+  }
+  if (r > e->cap_r) {
+    if (e->d_ids) CK(cudaFree(e->d_ids));
+    if (e->d_dists) CK(cudaFree(e->d_dists));
+    CK(cudaMalloc(&e->d_ids, r * 4));
+    CK(cudaMalloc(&e->d_dists, r * 4));
+    e->cap_r = r;
+  }
+  if (nq > e->cap_n) {
+    for (void* p : {(void*)e->d_found, (void*)e->d_steps, (void*)e->d_nbrs, (void*)e->d_time})
+      if (p) CK(cudaFree(p));
+    CK(cudaMalloc(&e->d_time, nq * 16));
+    CK(cudaMalloc(&e->d_found, nq * 4));
+    CK(cudaMalloc(&e->d_steps, nq * 4));
+    CK(cudaMalloc(&e->d_nbrs, nq * 8));
+    e->cap_n = nq;
+  }
+}
+
+float elapsed(cudaEvent_t a, cudaEvent_t b) {
+  float ms = 0.f;
+  CK(cudaEventElapsedTime(&ms, a, b));
+  return ms;
+}
+
+// --------------------------------------------------- component kernels --
+
+__global__ void lut_component_kernel(const qvk::SearchParams p, float* lut, float* q2) {
+  const int lane = threadIdx.x & 31;
+  const int64_t q = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  if (q >= p.nq) return;
+  qvk::build_lut_warp(p, p.queries + q * p.dim, lut + q * int64_t(p.M) * qvk::kPivots,
+                      q2 + q * p.dim, lane);
+}
+
+__global__ void adc_component_kernel(const uint8_t* __restrict__ codes, int M,
+                                     const float* __restrict__ lut, const int32_t* __restrict__ qof,
+                                     const int32_t* __restrict__ ids, int64_t n, float* out) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const float* t = lut + static_cast<int64_t>(qof[i]) * M * qvk::kPivots;
+  const uint8_t* c = codes + static_cast<int64_t>(ids[i]) * M;
+  float acc = 0.f;
+  for (int j = 0; j < M; ++j) acc = __fadd_rn(acc, t[j * qvk::kPivots + c[j]]);
+  out[i] = acc;
+}
+
+template <typename T>
+__global__ void l2_component_kernel(const qvk::SearchParams p, const float* q2, const int32_t* qof,
+                                    const int32_t* ids, int64_t n, float* out) {
+  const int lane = threadIdx.x & 31;
+  const int64_t i = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  if (i >= n) return;
+  const int64_t v = ids[i];
+  const T* vec = reinterpret_cast<const T*>(p.pages + (v / p.npp) * qvk::kPageSize +
+                                            (v % p.npp) * p.node_size);
+  const float d = qvk::exact_l2_warp<T>(q2 + static_cast<int64_t>(qof[i]) * p.dim, vec, p.dim, lane);
+  if (lane == 0) out[i] = d;
+}
+
+}  // namespace
+
+// ================================================================ C ABI ==
+
+extern "C" {
+
+const char* qv_version(void) { return "quiver-b200 0.1.0 (sm_100a)"; }
+
+const char* qv_last_error(void) { return g_last_error.c_str(); }
+
+void qv_search_opts_default(qv_search_opts* o) {
+  if (!o) return;
+  o->topk = 10;
+  o->ef_search = 30;
+  o->pipe_width = 2;
+  o->queries_per_block = 0;
+  o->num_blocks = 0;
+  o->early_exit_policy = QV_EXIT_GPRUNING;
+  o->gpruning_warmup_steps = 10;
+  o->gpruning_patience = 8;
+  o->lut_mode = QV_LUT_FP32;
+}
+
+int qv_engine_create(const qv_engine_opts* opts, qv_engine** out) {
+  return guarded([&] {
+    if (!opts || !out || !opts->index_dir) fail(QV_ERR_INVALID_ARG, "null argument");
+    *out = nullptr;
+    if (opts->data_type != QV_UINT8 && opts->data_type != QV_FLOAT && opts->data_type != QV_INT8)
+      fail(QV_ERR_INVALID_ARG, "data_type must be QV_UINT8, QV_FLOAT or QV_INT8");
+    const std::string dir = opts->index_dir;
+    const std::string backend = opts->memory_backend && *opts->memory_backend ? opts->memory_backend : "heap";
+    if (backend != "heap" && backend != "mmap")
+      fail(QV_ERR_INVALID_ARG, "Unsupported --memory-backend '" + backend + "'. Expected one of: heap, mmap");
+    const std::string index_file = qv::find_index_file(dir);
+    const std::string page_file =
+        opts->memory_index_file && *opts->memory_index_file ? opts->memory_index_file : index_file;
+    const std::string prefix = qv::find_pq_prefix(dir);
+    auto e = std::make_unique<qv_engine>();
+    e->L = qv::parse_disk_index_header(index_file, opts->data_type);
+    qv::PQTables pq = qv::read_pq(prefix + "_pivots.bin", prefix + "_compressed.bin");
+    qv::check_layout(e->L, &pq);
+    e->M = pq.num_chunks;
+    init_device_side(e.get(), opts->device);
+    alloc_pages(e.get(), opts->page_store);
+    const size_t bytes = static_cast<size_t>(e->L.num_pages) * qv::kPage;
+    if (e->pages_host) {
+      qv::read_pages(page_file, e->L.num_pages, backend, e->h_pages);
+      if (opts->validate) {
+        const int64_t b = qv::validate_adjacency(e->L, e->h_pages);
+        if (b >= 0) fail(QV_ERR_BAD_INDEX, "adjacency list of node " + std::to_string(b) + " is malformed");
+      }
+    } else {
+      std::vector<uint8_t> host(bytes);
+      qv::read_pages(page_file, e->L.num_pages, backend, host.data());
+      if (opts->validate) {
+        const int64_t b = qv::validate_adjacency(e->L, host.data());
+        if (b >= 0) fail(QV_ERR_BAD_INDEX, "adjacency list of node " + std::to_string(b) + " is malformed");
+      }
+      CK(cudaMemcpy(e->d_pages, host.data(), bytes, cudaMemcpyHostToDevice));
+    }
+    upload_pq(e.get(), pq.pivots.data(), pq.centroid.data(), pq.chunk_offsets.data(), pq.codes.data());
+    *out = e.release();
+  });
+}
+
+int qv_engine_create_from_arrays(const qv_index_arrays* a, int32_t device, int32_t page_store,
+                                 qv_engine** out) {
+  return guarded([&] {
+    if (!a || !out || !a->pages || !a->codes || !a->pivots || !a->centroid || !a->chunk_offsets)
+      fail(QV_ERR_INVALID_ARG, "null argument");
+    *out = nullptr;
+    auto e = std::make_unique<qv_engine>();
+    const auto& in = a->info;
+    if (in.data_type != QV_UINT8 && in.data_type != QV_FLOAT && in.data_type != QV_INT8)
+      fail(QV_ERR_INVALID_ARG, "data_type must be QV_UINT8, QV_FLOAT or QV_INT8");
+    e->L.num_points = in.num_points;
+    e->L.dim = in.dim;
+    e->L.data_type = in.data_type;
+    e->L.node_size = in.node_size;
+    e->L.data_size = in.dim * qv::element_size(in.data_type);
+    e->L.max_degree = (in.node_size - e->L.data_size) / 4 - 1;
+    e->L.nodes_per_page = in.nodes_per_page;
+    if (in.nodes_per_page <= 0) fail(QV_ERR_BAD_INDEX, "nodes_per_page must be positive");
+    e->L.num_pages = (in.num_points + in.nodes_per_page - 1) / in.nodes_per_page;
+    e->L.medoid = in.medoid;
+    e->M = in.num_chunks;
+    qv::PQTables shape;
+    shape.dim = static_cast<int32_t>(in.dim);
+    shape.num_chunks = in.num_chunks;
+    shape.num_points = in.num_points;
+    shape.chunk_offsets.assign(a->chunk_offsets, a->chunk_offsets + in.num_chunks + 1);
+    qv::check_layout(e->L, &shape);
+    init_device_side(e.get(), device);
+    alloc_pages(e.get(), page_store);
+    const size_t bytes = static_cast<size_t>(e->L.num_pages) * qv::kPage;
+    if (e->pages_host)
+      std::memcpy(e->h_pages, a->pages, bytes);
+    else
+      CK(cudaMemcpy(e->d_pages, a->pages, bytes, cudaMemcpyHostToDevice));
+    upload_pq(e.get(), a->pivots, a->centroid, a->chunk_offsets, a->codes);
+    *out = e.release();
+  });
+}
+
+int qv_engine_info(const qv_engine* e, qv_index_info* info) {
+  return guarded([&] {
+    if (!e || !info) fail(QV_ERR_INVALID_ARG, "null argument");
+    info->num_points = e->L.num_points;
+    info->dim = e->L.dim;
+    info->max_degree = e->L.max_degree;
+    info->node_size = e->L.node_size;
+    info->data_size = e->L.data_size;
+    info->nodes_per_page = e->L.nodes_per_page;
+    info->num_pages = e->L.num_pages;
+    info->medoid = e->L.medoid;
+    info->data_type = e->L.data_type;
+    info->num_chunks = e->M;
+  });
+}
+
+void qv_engine_destroy(qv_engine* e) { delete e; }
+
+int qv_plan(qv_engine* e, const qv_search_opts* opts, int64_t nq, qv_search_stats* plan) {
+  return guarded([&] {
+    if (!e || !opts || !plan) fail(QV_ERR_INVALID_ARG, "null argument");
+    CK(cudaSetDevice(e->device));
+    const Plan pl = make_plan(e, *opts, std::max<int64_t>(nq, 1));
+    std::memset(plan, 0, sizeof(*plan));
+    plan->grid = pl.grid;
+    plan->slots_per_block = pl.slots;
+    plan->smem_per_block = pl.smem;
+    plan->blocks_per_sm = pl.blocks_per_sm;
+  });
+}
+
+static int search_host(qv_engine* e, const float* queries, int64_t nq, int64_t dim, const qv_search_opts* opts,
+                       int32_t* ids, float* dists, int32_t* found, float* query_ms, qv_search_stats* stats) {
+  return guarded([&] {
+    if (!e || !opts || (nq > 0 && (!queries || !ids || !dists))) fail(QV_ERR_INVALID_ARG, "null argument");
+    if (nq < 0) fail(QV_ERR_INVALID_ARG, "nq must be non-negative");
+    if (dim != e->L.dim)
+      fail(QV_ERR_INVALID_ARG, "Query dimension mismatch: queries have " + std::to_string(dim) +
+                                   " dims, but the index expects " + std::to_string(e->L.dim));
+    const auto t0 = std::chrono::steady_clock::now();
+    CK(cudaSetDevice(e->device));
+    const Plan pl = make_plan(e, *opts, std::max<int64_t>(nq, 1));
+    if (stats) std::memset(stats, 0, sizeof(*stats));
+    if (nq == 0) return;
+    ensure_staging(e, nq, opts->topk);
+    const bool want_counts = stats != nullptr;
+    cudaStream_t st = e->stream;
+    CK(cudaEventRecord(e->ev[0], st));
+    CK(cudaMemcpyAsync(e->d_q, queries, nq * dim * 4, cudaMemcpyHostToDevice, st));
+    CK(cudaEventRecord(e->ev[1], st));
+    const auto p = make_params(e, pl, *opts, e->d_q, nq, e->d_ids, e->d_dists, e->d_found,
+                               want_counts ? e->d_steps : nullptr, want_counts ? e->d_nbrs : nullptr,
+                               query_ms ? e->d_time : nullptr);
+    enqueue_search(e, pl, p, st);
+    CK(cudaEventRecord(e->ev[2], st));
+    CK(cudaMemcpyAsync(ids, e->d_ids, nq * opts->topk * 4, cudaMemcpyDeviceToHost, st));
+    CK(cudaMemcpyAsync(dists, e->d_dists, nq * opts->topk * 4, cudaMemcpyDeviceToHost, st));
+    if (found) CK(cudaMemcpyAsync(found, e->d_found, nq * 4, cudaMemcpyDeviceToHost, st));
+    CK(cudaEventRecord(e->ev[3], st));
+    CK(cudaStreamSynchronize(st));
+    read_device_status(e);
+    if (query_ms) {
+      std::vector<int64_t> t(2 * nq);
+      CK(cudaMemcpy(t.data(), e->d_time, nq * 16, cudaMemcpyDeviceToHost));
+      for (int64_t i = 0; i < nq; ++i) query_ms[i] = static_cast<float>((t[2 * i + 1] - t[2 * i]) * 1e-6);
+    }
+    if (stats) {
+      stats->h2d_ms = elapsed(e->ev[0], e->ev[1]);
+      stats->kernel_ms = elapsed(e->ev[1], e->ev[2]);
+      stats->d2h_ms = elapsed(e->ev[2], e->ev[3]);
+      std::vector<int32_t> steps(nq);
+      std::vector<int64_t> nbrs(nq);
+      CK(cudaMemcpy(steps.data(), e->d_steps, nq * 4, cudaMemcpyDeviceToHost));
+      CK(cudaMemcpy(nbrs.data(), e->d_nbrs, nq * 8, cudaMemcpyDeviceToHost));
+      for (int64_t i = 0; i < nq; ++i) {
+        stats->expansions += steps[i];
+        stats->neighbors_scored += nbrs[i];
+      }
+      stats->grid = pl.grid;
+      stats->slots_per_block = pl.slots;
+      stats->smem_per_block = pl.smem;
+      stats->blocks_per_sm = pl.blocks_per_sm;
+      stats->total_ms =
+          std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+    }
+  });
+}
+
+int qv_search(qv_engine* e, const float* queries, int64_t nq, int64_t dim, const qv_search_opts* opts,
+              int32_t* ids, float* dists, int32_t* found, qv_search_stats* stats) {
+  return search_host(e, queries, nq, dim, opts, ids, dists, found, nullptr, stats);
+}
+
+int qv_search_timed(qv_engine* e, const float* queries, int64_t nq, int64_t dim, const qv_search_opts* opts,
+                    int32_t* ids, float* dists, int32_t* found, float* query_ms, qv_search_stats* stats) {
+  return search_host(e, queries, nq, dim, opts, ids, dists, found, query_ms, stats);
+}
+
+int qv_search_device(qv_engine* e, const float* d_queries, int64_t nq, const qv_search_opts* opts,
+                     int32_t* d_ids, float* d_dists, int32_t* d_found, int32_t* d_steps,
+                     int64_t* d_nbrs, void* stream) {
+  return guarded([&] {
+    if (!e || !opts || (nq > 0 && (!d_queries || !d_ids || !d_dists))) fail(QV_ERR_INVALID_ARG, "null argument");
+    if (nq < 0) fail(QV_ERR_INVALID_ARG, "nq must be non-negative");
+    CK(cudaSetDevice(e->device));
+    const Plan pl = make_plan(e, *opts, std::max<int64_t>(nq, 1));
+    if (nq == 0) return;
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : e->stream;
+    const auto p = make_params(e, pl, *opts, d_queries, nq, d_ids, d_dists, d_found, d_steps, d_nbrs);
+    enqueue_search(e, pl, p, st);
+  });
+}
+
+int qv_check_device_status(qv_engine* e) {
+  return guarded([&] {
+    if (!e) fail(QV_ERR_INVALID_ARG, "null argument");
+    CK(cudaSetDevice(e->device));
+    CK(cudaDeviceSynchronize());
+    read_device_status(e);
+  });
+}
+
+int qv_build_lut_device(qv_engine* e, const float* d_queries, int64_t nq, float* d_lut, float* d_q2,
+                        void* stream) {
+  return guarded([&] {
+    if (!e || (nq > 0 && (!d_queries || !d_lut || !d_q2))) fail(QV_ERR_INVALID_ARG, "null argument");
+    CK(cudaSetDevice(e->device));
+    if (nq <= 0) return;
+    qv_search_opts o;
+    qv_search_opts_default(&o);
+    qvk::SearchParams p{};
+    p.pivots_t = e->d_pivots_t;
+    p.centroid = e->d_centroid;
+    p.chunk_off = e->d_chunk_off;
+    p.queries = d_queries;
+    p.nq = nq;
+    p.dim = static_cast<int32_t>(e->L.dim);
+    p.M = e->M;
+    const int warps_per_block = 4;
+    const int64_t blocks = (nq + warps_per_block - 1) / warps_per_block;
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : e->stream;
+    lut_component_kernel<<<static_cast<unsigned>(blocks), warps_per_block * 32, 0, st>>>(p, d_lut, d_q2);
+    CK(cudaGetLastError());
+    if (!stream) CK(cudaStreamSynchronize(st));
+  });
+}
+
+int qv_adc_device(qv_engine* e, const float* d_lut, const int32_t* d_qof, const int32_t* d_ids, int64_t n,
+                  float* d_out, void* stream) {
+  return guarded([&] {
+    if (!e || (n > 0 && (!d_lut || !d_qof || !d_ids || !d_out))) fail(QV_ERR_INVALID_ARG, "null argument");
+    CK(cudaSetDevice(e->device));
+    if (n <= 0) return;
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : e->stream;
+    adc_component_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, st>>>(e->d_codes, e->M, d_lut,
+                                                                                 d_qof, d_ids, n, d_out);
+    CK(cudaGetLastError());
+    if (!stream) CK(cudaStreamSynchronize(st));
+  });
+}
+
+int qv_exact_l2_device(qv_engine* e, const float* d_q2, const int32_t* d_qof, const int32_t* d_ids, int64_t n,
+                       float* d_out, void* stream) {
+  return guarded([&] {
+    if (!e || (n > 0 && (!d_q2 || !d_qof || !d_ids || !d_out))) fail(QV_ERR_INVALID_ARG, "null argument");
+    CK(cudaSetDevice(e->device));
+    if (n <= 0) return;
+    qvk::SearchParams p{};
+    p.pages = e->d_pages;
+    p.dim = static_cast<int32_t>(e->L.dim);
+    p.npp = static_cast<int32_t>(e->L.nodes_per_page);
+    p.node_size = static_cast<int32_t>(e->L.node_size);
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : e->stream;
+    const unsigned blocks = static_cast<unsigned>((n * 32 + 255) / 256);
+    switch (e->L.data_type) {
+      case QV_UINT8: l2_component_kernel<uint8_t><<<blocks, 256, 0, st>>>(p, d_q2, d_qof, d_ids, n, d_out); break;
+      case QV_INT8: l2_component_kernel<int8_t><<<blocks, 256, 0, st>>>(p, d_q2, d_qof, d_ids, n, d_out); break;
+      default: l2_component_kernel<float><<<blocks, 256, 0, st>>>(p, d_q2, d_qof, d_ids, n, d_out); break;
+    }
+    CK(cudaGetLastError());
+    if (!stream) CK(cudaStreamSynchronize(st));
+  });
+}
+
+}  // extern "C"

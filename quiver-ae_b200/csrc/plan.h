@@ -1,0 +1,50 @@
+// plan.h -- launch plan shared by the engine and the per-type kernel units.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include "search_kernel.cuh"
+
+namespace qv {
+
+struct Plan {
+  qvk::SlotLayout lay;
+  int smax = 2;         // neighbours per lane (R <= 32 * smax)
+  int mc = 0;           // PQ code width the kernel is specialised for (0 = any)
+  int slots = 1;        // query slots (warps) per CTA
+  int blocks_per_sm = 0;
+  int grid = 0;
+  int smem = 0;
+  const void* fn = nullptr;
+  void (*launch)(const qvk::SearchParams&, int grid, int block, int smem, cudaStream_t) = nullptr;
+};
+
+// Defined in search_u8.cu / search_i8.cu / search_f32.cu: pick the kernel
+// instantiation for pl.mc and pl.smax.
+void bind_search_u8(Plan& pl);
+void bind_search_i8(Plan& pl);
+void bind_search_f32(Plan& pl);
+
+template <typename T, int MC, int SMAX>
+void launch_search(const qvk::SearchParams& p, int grid, int block, int smem, cudaStream_t st) {
+  qvk::search_kernel<T, MC, SMAX><<<grid, block, smem, st>>>(p);
+}
+
+template <typename T, int MC, int SMAX>
+void bind_one(Plan& pl) {
+  pl.fn = reinterpret_cast<const void*>(&qvk::search_kernel<T, MC, SMAX>);
+  pl.launch = &launch_search<T, MC, SMAX>;
+}
+
+// PQ widths with a register-blocked code path; any other M uses MC = 0.
+template <typename T>
+void bind_type(Plan& pl) {
+  if (pl.mc == 32) {
+    if (pl.smax == 2) bind_one<T, 32, 2>(pl); else bind_one<T, 32, 4>(pl);
+  } else {
+    pl.mc = 0;
+    if (pl.smax == 2) bind_one<T, 0, 2>(pl); else bind_one<T, 0, 4>(pl);
+  }
+}
+
+}  // namespace qv

@@ -1,0 +1,116 @@
+"""Synthetic inputs and index construction (host library ``libqv_index.so``).
+
+The reference builds indexes with DiskANN (an empty submodule here), so this
+module writes the same files from its own Vamana + PQ implementation, and
+generates the seeded Gaussian-mixture data that stands in for SIFT/DEEP.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass
+from pathlib import Path
+
+import numpy as np
+
+from . import _lib, formats
+
+
+def _check(rc: int) -> None:
+    if rc != _lib.QV_OK:
+        msg = _lib.index_lib().qvb_last_error().decode()
+        raise RuntimeError(f"libqv_index error {rc}: {msg}")
+
+
+def _ptr(a: np.ndarray) -> C.c_void_p:
+    return C.c_void_p(a.ctypes.data)
+
+
+def synth_mixture(seed: int, n: int, dim: int, n_centers: int, sigma: float, data_type: str = "uint8",
+                  stream: int = 0, row0: int = 0, nthreads: int = 0) -> np.ndarray:
+    """Rows [row0, row0+n) of the seeded mixture (stream 0 = base, 1 = queries)."""
+    dt = formats.NUMPY_DTYPES[data_type]
+    out = np.empty((n, dim), dtype=dt)
+    _check(_lib.index_lib().qvb_synth_mixture(seed, stream, row0, n, dim, n_centers, sigma,
+                                               _lib.DTYPE_CODES[data_type], _ptr(out), nthreads))
+    return out
+
+
+def ground_truth(base: np.ndarray, queries: np.ndarray, k: int, nthreads: int = 0) -> tuple[np.ndarray, np.ndarray]:
+    """Exact squared-L2 top-k (ties by lower id)."""
+    base = np.ascontiguousarray(base)
+    queries = np.ascontiguousarray(queries, dtype=base.dtype)
+    dtype = {np.dtype(np.uint8): _lib.QV_UINT8, np.dtype(np.int8): _lib.QV_INT8,
+             np.dtype(np.float32): _lib.QV_FLOAT}[base.dtype]
+    ids = np.empty((queries.shape[0], k), dtype=np.int32)
+    dists = np.empty((queries.shape[0], k), dtype=np.float32)
+    _check(_lib.index_lib().qvb_ground_truth(_ptr(base), base.shape[0], _ptr(queries), queries.shape[0],
+                                              base.shape[1], dtype, k, _ptr(ids), _ptr(dists), nthreads))
+    return ids, dists
+
+
+@dataclass
+class BuiltIndex:
+    index_dir: Path
+    prefix: Path
+    data_type: str
+    layout: formats.DiskLayout
+
+
+def vamana(base: np.ndarray, R: int, L: int, alpha: float, passes: int = 2, seed: int = 0,
+           nthreads: int = 0) -> tuple[np.ndarray, np.ndarray, int]:
+    base = np.ascontiguousarray(base)
+    n, dim = base.shape
+    dtype = {np.dtype(np.uint8): _lib.QV_UINT8, np.dtype(np.int8): _lib.QV_INT8,
+             np.dtype(np.float32): _lib.QV_FLOAT}[base.dtype]
+    graph = np.empty((n, R), dtype=np.int32)
+    degree = np.empty(n, dtype=np.int32)
+    medoid = C.c_int64(0)
+    _check(_lib.index_lib().qvb_vamana(_ptr(base), n, dim, dtype, R, L, alpha, passes, seed, nthreads,
+                                        _ptr(graph), _ptr(degree), C.byref(medoid)))
+    return graph, degree, int(medoid.value)
+
+
+def pq_train(base: np.ndarray, M: int, sample: int = 100_000, iters: int = 12, seed: int = 0,
+             nthreads: int = 0) -> tuple[np.ndarray, np.ndarray, np.ndarray]:
+    base = np.ascontiguousarray(base)
+    n, dim = base.shape
+    dtype = {np.dtype(np.uint8): _lib.QV_UINT8, np.dtype(np.int8): _lib.QV_INT8,
+             np.dtype(np.float32): _lib.QV_FLOAT}[base.dtype]
+    pivots = np.empty((256, dim), dtype=np.float32)
+    centroid = np.empty(dim, dtype=np.float32)
+    offs = np.empty(M + 1, dtype=np.int32)
+    _check(_lib.index_lib().qvb_pq_train(_ptr(base), n, dim, dtype, M, sample, iters, seed, nthreads,
+                                          _ptr(pivots), _ptr(centroid), _ptr(offs)))
+    return pivots, centroid, offs
+
+
+def pq_encode(base: np.ndarray, pivots: np.ndarray, centroid: np.ndarray, chunk_offsets: np.ndarray,
+              nthreads: int = 0) -> np.ndarray:
+    base = np.ascontiguousarray(base)
+    n, dim = base.shape
+    M = len(chunk_offsets) - 1
+    dtype = {np.dtype(np.uint8): _lib.QV_UINT8, np.dtype(np.int8): _lib.QV_INT8,
+             np.dtype(np.float32): _lib.QV_FLOAT}[base.dtype]
+    codes = np.empty((n, M), dtype=np.uint8)
+    _check(_lib.index_lib().qvb_pq_encode(_ptr(base), n, dim, dtype, M,
+                                           _ptr(np.ascontiguousarray(pivots, dtype=np.float32)),
+                                           _ptr(np.ascontiguousarray(centroid, dtype=np.float32)),
+                                           _ptr(np.ascontiguousarray(chunk_offsets, dtype=np.int32)),
+                                           nthreads, _ptr(codes)))
+    return codes
+
+
+def build_index(index_dir: str | Path, base: np.ndarray, *, R: int = 64, L: int = 100, alpha: float = 1.2,
+                M: int = 32, passes: int = 2, pq_sample: int = 100_000, pq_iters: int = 12, seed: int = 0,
+                prefix: str = "ann", nthreads: int = 0) -> BuiltIndex:
+    """Write ``<prefix>_disk.index``, ``<prefix>_pq_pivots.bin`` and ``<prefix>_pq_compressed.bin``."""
+    index_dir = Path(index_dir)
+    index_dir.mkdir(parents=True, exist_ok=True)
+    base = np.ascontiguousarray(base)
+    data_type = {np.dtype(np.uint8): "uint8", np.dtype(np.int8): "int8", np.dtype(np.float32): "float"}[base.dtype]
+    graph, degree, medoid = vamana(base, R, L, alpha, passes, seed, nthreads)
+    layout = formats.write_disk_index(index_dir / f"{prefix}_disk.index", base, graph, degree, medoid, R)
+    pivots, centroid, offs = pq_train(base, M, pq_sample, pq_iters, seed, nthreads)
+    codes = pq_encode(base, pivots, centroid, offs, nthreads)
+    formats.write_pq(index_dir / prefix, pivots, centroid, offs, codes)
+    return BuiltIndex(index_dir, index_dir / prefix, data_type, layout)

@@ -1,0 +1,184 @@
+"""Python handle on the C ABI engine (include/quiver_b200.h).
+
+``Engine.search`` is the host-buffer call (``qv_search``); ``Engine.search_device``
+takes CUDA tensors already resident on the engine's GPU (``qv_search_device``).
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass
+from pathlib import Path
+
+import numpy as np
+
+from . import _lib, formats
+
+
+class QuiverEngineError(RuntimeError):
+    def __init__(self, code: int, message: str):
+        super().__init__(f"[qv error {code}] {message}")
+        self.code = code
+
+
+def _check(rc: int) -> None:
+    if rc != _lib.QV_OK:
+        raise QuiverEngineError(rc, _lib.engine_lib().qv_last_error().decode(errors="replace"))
+
+
+@dataclass
+class SearchParams:
+    topk: int = 10
+    ef_search: int = 30
+    pipe_width: int = 2
+    queries_per_block: int = 0
+    num_blocks: int = 0
+    early_exit_policy: str = "gpruning"
+    gpruning_warmup_steps: int = 10
+    gpruning_patience: int = 8
+    lut_mode: int = _lib.QV_LUT_FP32
+
+    def to_c(self) -> _lib.SearchOpts:
+        pol = {"none": _lib.QV_EXIT_NONE, "gpruning": _lib.QV_EXIT_GPRUNING}[self.early_exit_policy]
+        return _lib.SearchOpts(self.topk, self.ef_search, self.pipe_width, self.queries_per_block,
+                               self.num_blocks, pol, self.gpruning_warmup_steps, self.gpruning_patience,
+                               self.lut_mode)
+
+
+class Engine:
+    """One index resident on one GPU."""
+
+    def __init__(self, handle: C.c_void_p):
+        self._h = handle
+        self._lib = _lib.engine_lib()
+
+    @classmethod
+    def open(cls, index_dir: str | Path, data_type: str = "uint8", *, memory_backend: str = "heap",
+             memory_index_file: str | None = None, device: int = 0, page_store: str = "hbm",
+             validate: bool = False) -> "Engine":
+        lib = _lib.engine_lib()
+        opts = _lib.EngineOpts(str(index_dir).encode(), _lib.DTYPE_CODES[data_type], memory_backend.encode(),
+                               memory_index_file.encode() if memory_index_file else None, device,
+                               {"hbm": _lib.QV_PAGES_HBM, "host": _lib.QV_PAGES_HOST}[page_store],
+                               1 if validate else 0)
+        h = C.c_void_p()
+        _check(lib.qv_engine_create(C.byref(opts), C.byref(h)))
+        return cls(h)
+
+    @classmethod
+    def from_arrays(cls, *, data_type: str, num_points: int, dim: int, node_size: int, nodes_per_page: int,
+                    medoid: int, pages: np.ndarray, codes: np.ndarray, pivots: np.ndarray, centroid: np.ndarray,
+                    chunk_offsets: np.ndarray, device: int = 0, page_store: str = "hbm") -> "Engine":
+        lib = _lib.engine_lib()
+        keep = [np.ascontiguousarray(pages, dtype=np.uint8), np.ascontiguousarray(codes, dtype=np.uint8),
+                np.ascontiguousarray(pivots, dtype=np.float32), np.ascontiguousarray(centroid, dtype=np.float32),
+                np.ascontiguousarray(chunk_offsets, dtype=np.int32)]
+        info = _lib.IndexInfo(num_points, dim, 0, node_size, 0, nodes_per_page, 0, medoid,
+                              _lib.DTYPE_CODES[data_type], len(chunk_offsets) - 1)
+        arr = _lib.IndexArrays(info, *[C.c_void_p(a.ctypes.data) for a in keep])
+        h = C.c_void_p()
+        _check(lib.qv_engine_create_from_arrays(C.byref(arr), device,
+                                                {"hbm": _lib.QV_PAGES_HBM, "host": _lib.QV_PAGES_HOST}[page_store],
+                                                C.byref(h)))
+        return cls(h)
+
+    def close(self) -> None:
+        if self._h:
+            self._lib.qv_engine_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    @property
+    def info(self) -> _lib.IndexInfo:
+        i = _lib.IndexInfo()
+        _check(self._lib.qv_engine_info(self._h, C.byref(i)))
+        return i
+
+    def plan(self, params: SearchParams, nq: int) -> _lib.SearchStats:
+        st = _lib.SearchStats()
+        o = params.to_c()
+        _check(self._lib.qv_plan(self._h, C.byref(o), nq, C.byref(st)))
+        return st
+
+    def search(self, queries: np.ndarray, params: SearchParams | None = None, *, out=None,
+               with_stats: bool = False):
+        """Host buffers in and out: returns (ids [nq,k] i32, dists [nq,k] f32, found [nq] i32[, stats])."""
+        params = params or SearchParams()
+        q = np.ascontiguousarray(queries, dtype=np.float32)
+        if q.ndim == 1:
+            q = q.reshape(1, -1)
+        nq, dim = q.shape
+        k = params.topk
+        if out is None:
+            ids = np.empty((nq, k), dtype=np.int32)
+            dists = np.empty((nq, k), dtype=np.float32)
+            found = np.empty(nq, dtype=np.int32)
+        else:
+            ids, dists, found = out
+        st = _lib.SearchStats()
+        o = params.to_c()
+        _check(self._lib.qv_search(self._h, C.c_void_p(q.ctypes.data), nq, dim, C.byref(o),
+                                   C.c_void_p(ids.ctypes.data), C.c_void_p(dists.ctypes.data),
+                                   C.c_void_p(found.ctypes.data), C.byref(st) if with_stats else None))
+        if with_stats:
+            return ids, dists, found, st
+        return ids, dists, found
+
+    def search_host_ptrs(self, q_ptr: int, nq: int, dim: int, params: SearchParams, ids_ptr: int,
+                         dists_ptr: int, found_ptr: int | None = None) -> None:
+        """qv_search on raw host pointers (e.g. pinned torch tensors)."""
+        o = params.to_c()
+        _check(self._lib.qv_search(self._h, C.c_void_p(q_ptr), nq, dim, C.byref(o), C.c_void_p(ids_ptr),
+                                   C.c_void_p(dists_ptr), C.c_void_p(found_ptr) if found_ptr else None, None))
+
+    def search_device(self, d_queries, params: SearchParams, d_ids, d_dists, d_found=None, d_steps=None,
+                      d_nbrs=None, stream=None) -> None:
+        """Enqueue a search on CUDA tensors (torch) without synchronising."""
+        o = params.to_c()
+
+        def ptr(t):
+            return C.c_void_p(t.data_ptr()) if t is not None else None
+
+        st = C.c_void_p(stream) if stream else None
+        _check(self._lib.qv_search_device(self._h, ptr(d_queries), d_queries.shape[0], C.byref(o), ptr(d_ids),
+                                          ptr(d_dists), ptr(d_found), ptr(d_steps), ptr(d_nbrs), st))
+
+    def check_device_status(self) -> None:
+        _check(self._lib.qv_check_device_status(self._h))
+
+    # component kernels (torch CUDA tensors) -------------------------------
+    def build_lut(self, d_queries, d_lut, d_q2) -> None:
+        _check(self._lib.qv_build_lut_device(self._h, C.c_void_p(d_queries.data_ptr()), d_queries.shape[0],
+                                             C.c_void_p(d_lut.data_ptr()), C.c_void_p(d_q2.data_ptr()), None))
+
+    def adc(self, d_lut, d_query_of, d_ids, d_out) -> None:
+        _check(self._lib.qv_adc_device(self._h, C.c_void_p(d_lut.data_ptr()), C.c_void_p(d_query_of.data_ptr()),
+                                       C.c_void_p(d_ids.data_ptr()), d_ids.shape[0], C.c_void_p(d_out.data_ptr()),
+                                       None))
+
+    def exact_l2(self, d_q2, d_query_of, d_ids, d_out) -> None:
+        _check(self._lib.qv_exact_l2_device(self._h, C.c_void_p(d_q2.data_ptr()), C.c_void_p(d_query_of.data_ptr()),
+                                            C.c_void_p(d_ids.data_ptr()), d_ids.shape[0],
+                                            C.c_void_p(d_out.data_ptr()), None))
+
+
+def open_index_arrays(index_dir: str | Path, data_type: str) -> dict:
+    """Read an index directory into host arrays (for Engine.from_arrays)."""
+    index_dir = Path(index_dir)
+    disk = sorted(index_dir.glob("*_disk.index"))
+    piv = sorted(index_dir.glob("*_pq_pivots.bin"))
+    if len(disk) != 1 or len(piv) != 1:
+        raise FileNotFoundError(f"expected one *_disk.index and one *_pq_pivots.bin in {index_dir}")
+    lay = formats.read_disk_index_header(disk[0], data_type)
+    pq = formats.read_pq(str(piv[0])[: -len("_pq_pivots.bin")])
+    return {"layout": lay, "pages": formats.read_pages(disk[0], lay.num_pages), **pq}

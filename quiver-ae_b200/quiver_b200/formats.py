@@ -1,0 +1,167 @@
+"""DiskANN-layout files that Quiver's search reads, as numpy arrays.
+
+Layouts (paths inside ruc-system/quiver-ae):
+
+* ``*_disk.index`` -- page 0 holds the metadata bin read by
+  ``parse_diskann_metadata`` (bin/common/metadata.hpp:15-72): u32 nr, u32 nc,
+  then u64 N, dim, medoid, max_node_len, nodes_per_sector, num_frozen,
+  frozen_id, reorder_flag (+ file size).  Page p+1 holds nodes
+  [p*npp, (p+1)*npp); a node record is the vector, u32 degree, u32[R]
+  neighbour ids, zero padded (node_size = dim*elem + 4*(R+1)).
+* ``*_pq_pivots.bin`` -- a 4x1 u64 offsets bin at 0; pivots [256 x dim] f32,
+  centroid [dim x 1] f32 and chunk offsets [(M+1) x 1] i32 at those offsets
+  (src/shared/index/pq_search.cu:62-114).
+* ``*_pq_compressed.bin`` -- [N x M] u8 codes.
+* ``.u8bin`` / ``.i8bin`` / ``.fbin`` / ``.ibin`` -- i32 n, i32 d, row-major data
+  (bin/common/data_io.hpp:23-133).
+"""
+from __future__ import annotations
+
+import struct
+from dataclasses import dataclass
+from pathlib import Path
+
+import numpy as np
+
+PAGE = 4096
+NUMPY_DTYPES = {"uint8": np.uint8, "int8": np.int8, "float": np.float32, "float32": np.float32}
+
+
+@dataclass
+class DiskLayout:
+    num_points: int
+    dim: int
+    medoid: int
+    node_size: int
+    nodes_per_page: int
+    data_size: int
+    max_degree: int
+    num_pages: int
+
+
+def write_bin(path: str | Path, arr: np.ndarray) -> None:
+    arr = np.ascontiguousarray(arr)
+    if arr.ndim != 2:
+        raise ValueError("bin files hold 2-D arrays")
+    with open(path, "wb") as f:
+        f.write(struct.pack("<ii", arr.shape[0], arr.shape[1]))
+        f.write(arr.tobytes())
+
+
+def read_bin(path: str | Path, dtype) -> np.ndarray:
+    with open(path, "rb") as f:
+        n, d = struct.unpack("<ii", f.read(8))
+        data = np.fromfile(f, dtype=dtype, count=n * d)
+    if data.size != n * d:
+        raise ValueError(f"truncated bin file {path}")
+    return data.reshape(n, d)
+
+
+def node_size_for(dim: int, dtype, R: int) -> int:
+    return dim * np.dtype(dtype).itemsize + 4 * (R + 1)
+
+
+def build_pages(data: np.ndarray, graph: np.ndarray, degree: np.ndarray, R: int) -> tuple[np.ndarray, int, int]:
+    """Node records packed into 4 KB pages -> (pages [P x 4096] u8, node_size, npp)."""
+    n, dim = data.shape
+    data_size = dim * data.dtype.itemsize
+    node_size = data_size + 4 * (R + 1)
+    npp = PAGE // node_size
+    if npp < 1:
+        raise ValueError("a node record does not fit in a 4 KB page")
+    rec = np.zeros((n, node_size), dtype=np.uint8)
+    rec[:, :data_size] = np.ascontiguousarray(data).view(np.uint8).reshape(n, data_size)
+    rec[:, data_size:data_size + 4] = degree.astype("<u4").view(np.uint8).reshape(n, 4)
+    nb = np.where(np.arange(R)[None, :] < degree[:, None], graph[:, :R], 0).astype("<u4")
+    rec[:, data_size + 4:] = nb.view(np.uint8).reshape(n, 4 * R)
+    num_pages = (n + npp - 1) // npp
+    pages = np.zeros((num_pages, PAGE), dtype=np.uint8)
+    full = np.zeros((num_pages * npp, node_size), dtype=np.uint8)
+    full[:n] = rec
+    pages[:, :npp * node_size] = full.reshape(num_pages, npp * node_size)
+    return pages, node_size, npp
+
+
+def write_disk_index(path: str | Path, data: np.ndarray, graph: np.ndarray, degree: np.ndarray,
+                     medoid: int, R: int) -> DiskLayout:
+    n, dim = data.shape
+    pages, node_size, npp = build_pages(data, graph, degree, R)
+    file_size = PAGE * (pages.shape[0] + 1)
+    meta = [n, dim, medoid, node_size, npp, 0, 0, 0, file_size]
+    header = np.zeros(PAGE, dtype=np.uint8)
+    hb = struct.pack("<II", len(meta), 1) + struct.pack(f"<{len(meta)}Q", *meta)
+    header[:len(hb)] = np.frombuffer(hb, dtype=np.uint8)
+    with open(path, "wb") as f:
+        f.write(header.tobytes())
+        f.write(pages.tobytes())
+    return DiskLayout(n, dim, medoid, node_size, npp, dim * data.dtype.itemsize, R, pages.shape[0])
+
+
+def read_disk_index_header(path: str | Path, data_type: str) -> DiskLayout:
+    with open(path, "rb") as f:
+        nr, nc = struct.unpack("<II", f.read(8))
+        n, dim, medoid, node_size, npp, _, _, _ = struct.unpack("<8Q", f.read(64))
+    elem = np.dtype(NUMPY_DTYPES[data_type]).itemsize
+    data_size = dim * elem
+    R = (node_size - data_size) // 4 - 1
+    return DiskLayout(n, dim, medoid, node_size, npp, data_size, R, (n + npp - 1) // npp)
+
+
+def read_pages(path: str | Path, num_pages: int) -> np.ndarray:
+    with open(path, "rb") as f:
+        f.seek(PAGE)
+        pages = np.fromfile(f, dtype=np.uint8, count=num_pages * PAGE)
+    if pages.size != num_pages * PAGE:
+        raise ValueError(f"page store of {path} is truncated")
+    return pages.reshape(num_pages, PAGE)
+
+
+def write_pq(prefix: str | Path, pivots: np.ndarray, centroid: np.ndarray, chunk_offsets: np.ndarray,
+             codes: np.ndarray) -> None:
+    """Write ``<prefix>_pq_pivots.bin`` (4-entry offsets layout) and ``<prefix>_pq_compressed.bin``."""
+    pivots = np.ascontiguousarray(pivots, dtype="<f4")
+    centroid = np.ascontiguousarray(centroid, dtype="<f4").reshape(-1, 1)
+    chunk_offsets = np.ascontiguousarray(chunk_offsets, dtype="<i4").reshape(-1, 1)
+    blobs = [pivots, centroid, chunk_offsets]
+    offs = [PAGE]
+    for b in blobs:
+        offs.append(offs[-1] + 8 + b.nbytes)
+    with open(f"{prefix}_pq_pivots.bin", "wb") as f:
+        meta = struct.pack("<ii", 4, 1) + struct.pack("<4Q", *offs)
+        f.write(meta + b"\0" * (PAGE - len(meta)))
+        for b in blobs:
+            f.write(struct.pack("<ii", b.shape[0], b.shape[1]))
+            f.write(b.tobytes())
+    write_bin(f"{prefix}_pq_compressed.bin", np.ascontiguousarray(codes, dtype=np.uint8))
+
+
+def read_pq(prefix: str | Path) -> dict:
+    with open(f"{prefix}_pq_pivots.bin", "rb") as f:
+        nr, nc = struct.unpack("<ii", f.read(8))
+        offs = struct.unpack(f"<{nr}Q", f.read(8 * nr))
+        chunk_idx = 3 if nr == 5 else 2
+
+        def at(off, dtype):
+            f.seek(off)
+            r, c = struct.unpack("<ii", f.read(8))
+            return np.fromfile(f, dtype=dtype, count=r * c).reshape(r, c)
+
+        pivots = at(offs[0], "<f4")
+        centroid = at(offs[1], "<f4").reshape(-1)
+        chunk_offsets = at(offs[chunk_idx], "<i4").reshape(-1)
+    codes = read_bin(f"{prefix}_pq_compressed.bin", np.uint8)
+    return {"pivots": pivots, "centroid": centroid, "chunk_offsets": chunk_offsets, "codes": codes}
+
+
+def load_queries_as_float(path: str | Path, repeat: int = 1) -> np.ndarray:
+    """bin/common/data_io.hpp:73-108: the element type follows the file name."""
+    name = str(path)
+    if ".u8bin" in name:
+        q = read_bin(path, np.uint8).astype(np.float32)
+    elif ".i8bin" in name:
+        q = read_bin(path, np.int8).astype(np.float32)
+    else:
+        q = read_bin(path, np.float32)
+    if repeat > 1:
+        q = np.tile(q, (repeat, 1))
+    return np.ascontiguousarray(q)
