@@ -1,0 +1,357 @@
+#!/usr/bin/env python
+"""Throughput of Quiver's query hot path on B200.
+
+One step = one search pass over one batch of synthetic queries (10K rows of
+the workload's query stream) against the workload's index, top-10, at the
+smallest ef_search from a fixed ladder whose Recall@10 reaches the target
+(0.90 by default).  Prints one JSON line on rank 0.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+N > 1 runs under torchrun: each rank holds a replica of the index and
+searches its own 10K-query batch per step (weak scaling, no collective on
+the data path; the barrier and the max-over-ranks timing use NCCL).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from datetime import timedelta
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "quiver-ae_b200"))
+sys.path.insert(0, str(ROOT))
+
+METRIC = "QPS at Recall@10=0.90 and P99 latency (ms), 1/2/4/8 B200, 1B×128 uint8"
+EF_LADDER = (45, 60, 80, 100, 120, 150, 180, 220, 260, 320, 400)
+CALIB_QUERIES = 2000
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+def workload_desc(w) -> str:
+    return (f"{w.name}: {w.n // 1_000_000 if w.n >= 1_000_000 else w.n}{'M' if w.n >= 1_000_000 else ''} x {w.dim}-d "
+            f"{w.data_type} seeded {w.centers}-cluster Gaussian mixture (sigma {w.sigma}); Vamana R={w.R} "
+            f"L={w.L} alpha={w.alpha}; PQ M={w.M} x 256; {w.nq} queries per step; top-{w.topk}")
+
+
+def pick_ef(recall_of, target: float) -> tuple[int, float]:
+    """Smallest ladder ef whose Recall@10 reaches the target (else the largest)."""
+    r = 0.0
+    for ef in EF_LADDER:
+        r = recall_of(ef)
+        if r >= target:
+            return ef, r
+    return EF_LADDER[-1], r
+
+
+def read_peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": float(d["hbm_gbs"]), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "source": "fallback"}
+
+
+def read_profile_traffic(name: str) -> float | None:
+    """dram bytes per launch from a committed ncu summary (key: value lines)."""
+    p = ROOT / "profiles" / name
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        if line.startswith("dram_bytes_per_launch_scaled:"):
+            try:
+                return float(line.split(":", 1)[1].strip())
+            except ValueError:
+                return None
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons during the timed region."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.proc = None
+        self.tmp = None
+
+    def __enter__(self):
+        self.tmp = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-i", str(self.device), "-lms", "100"], stdout=self.tmp,
+                                         stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.25)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            time.sleep(0.15)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        rows = []
+        try:
+            for line in Path(self.tmp.name).read_text().splitlines():
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        finally:
+            os.unlink(self.tmp.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        smax = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def reference_arm(args, rank: int, world: int) -> int:
+    """The reference's CPU implementation of the path, on the host cores.
+
+    The reference ships no CPU search (its DiskANN submodule is empty), so
+    this arm runs the oracle -- the C restatement of the reference kernel's
+    semantics -- with every host thread, on the same index, queries and ef."""
+    if rank != 0:
+        return 0
+    from oracle import pyoracle
+    from quiver_b200 import workloads
+    w = workloads.CONFIGS[args.config]
+    d = workloads.prepare(w, log=log)
+    ix = pyoracle.load_index(d, w.data_type)
+    qc = workloads.queries(w, rows=CALIB_QUERIES).astype(np.float32)
+    gtc = workloads.ground_truth(w, qc, 10)
+    search_kw = dict(topk=w.topk, pipe_width=args.pipe_width, early_exit_policy=args.early_exit)
+    if args.ef > 0:
+        ef = args.ef
+        recall = pyoracle.calc_recall(pyoracle.search(ix, qc, ef_search=ef, **search_kw)["ids"], gtc, 10)
+    else:
+        ef, recall = pick_ef(lambda e: pyoracle.calc_recall(pyoracle.search(ix, qc, ef_search=e, **search_kw)["ids"],
+                                                            gtc, 10), args.target_recall)
+    q = workloads.queries(w).astype(np.float32)
+    cores = os.cpu_count() or 1
+    # size each step to ~0.5 s of host work so K steps end within minutes
+    t = time.perf_counter()
+    pyoracle.search(ix, q[:256], ef_search=ef, **search_kw)
+    rate = 256 / max(time.perf_counter() - t, 1e-6)
+    per_step = int(min(w.nq, max(64, rate * 0.5)))
+    for i in range(args.warmup):
+        pyoracle.search(ix, q[:per_step], ef_search=ef, **search_kw)
+    t = time.perf_counter()
+    for i in range(args.steps):
+        s0 = (i * per_step) % max(1, w.nq - per_step + 1)
+        pyoracle.search(ix, q[s0:s0 + per_step], ef_search=ef, **search_kw)
+    dt = time.perf_counter() - t
+    qps = args.steps * per_step / dt
+    sample = f"{per_step} of the {w.nq} queries per step, ef_search={ef}, pipe_width={args.pipe_width}"
+    line = {
+        "impl": "reference", "metric": METRIC, "value": qps, "unit": "queries/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1000 / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded Gaussian mixture; SIFT/DEEP not present)",
+        "config": {"workload": workload_desc(w), "ef_search": ef, "recall_at_10": recall,
+                   "pipe_width": args.pipe_width, "early_exit": args.early_exit},
+        "cpu_baseline": {"value": qps, "unit": "queries/s", "cores": cores, "kind": "port", "sample": sample},
+        "e2e": {"value": qps, "unit": "queries/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "recall_at_10": recall,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def cpu_baseline(w, d, ef: int, args) -> dict:
+    """The oracle on a bounded sample, all host threads, N=1 rank 0 only."""
+    from oracle import pyoracle
+    from quiver_b200 import workloads
+    ix = pyoracle.load_index(d, w.data_type)
+    q = workloads.queries(w).astype(np.float32)
+    kw = dict(topk=w.topk, ef_search=ef, pipe_width=args.pipe_width, early_exit_policy=args.early_exit)
+    t = time.perf_counter()
+    pyoracle.search(ix, q[:256], **kw)
+    rate = 256 / max(time.perf_counter() - t, 1e-6)
+    n = int(min(w.nq, max(256, rate * 12.0)))
+    t = time.perf_counter()
+    pyoracle.search(ix, q[:n], **kw)
+    dt = time.perf_counter() - t
+    return {"value": n / dt, "unit": "queries/s", "cores": os.cpu_count() or 1, "kind": "port",
+            "sample": f"first {n} of the {w.nq} step queries, ef_search={ef}, {dt:.1f} s of host work"}
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--config", default="config0")
+    ap.add_argument("--ef", type=int, default=0, help="fixed ef_search (0: smallest ladder ef reaching the target)")
+    ap.add_argument("--target-recall", type=float, default=0.90)
+    ap.add_argument("--pipe-width", type=int, default=2)
+    ap.add_argument("--early-exit", default="none", choices=["none", "gpruning"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        return reference_arm(args, rank, world)
+
+    import torch
+    import torch.distributed as dist
+    from quiver_b200 import Engine, SearchParams, shard, workloads
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=900), device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+        torch.cuda.synchronize()
+
+    w = workloads.CONFIGS[args.config]
+    if rank == 0:
+        workloads.prepare(w, log=log)
+    barrier()
+    d = workloads.index_dir(w)
+    eng = Engine.open(d, w.data_type, device=local)
+
+    # ef calibration on the first CALIB_QUERIES rows (identical on every rank)
+    qc = workloads.queries(w, rows=CALIB_QUERIES)
+    if rank == 0:
+        workloads.ground_truth(w, qc, 10, device=f"cuda:{local}")
+    barrier()
+    gtc = workloads.ground_truth(w, qc, 10)
+    from quiver_b200.recall import calc_recall
+
+    def params(ef):
+        return SearchParams(topk=w.topk, ef_search=ef, pipe_width=args.pipe_width, early_exit_policy=args.early_exit)
+
+    def recall_of(ef):
+        return calc_recall(eng.search(qc, params(ef))[0], gtc, 10)
+
+    if args.ef > 0:
+        ef, recall = args.ef, recall_of(args.ef)
+    else:
+        ef, recall = pick_ef(recall_of, args.target_recall)
+    p = params(ef)
+
+    # this rank's step batch, resident in HBM
+    row0, rows = shard.weak_rows(rank, w.nq)
+    q = workloads.queries(w, rows=rows, row0=row0).astype(np.float32)
+    nq, k = q.shape[0], w.topk
+    dq = torch.from_numpy(q).to(dev)
+    d_ids = torch.empty((nq, k), dtype=torch.int32, device=dev)
+    d_dists = torch.empty((nq, k), dtype=torch.float32, device=dev)
+    d_steps = torch.empty(nq, dtype=torch.int32, device=dev)
+    d_nbrs = torch.empty(nq, dtype=torch.int64, device=dev)
+    stream = torch.cuda.Stream(dev)  # every launch, event and copy of the step runs here
+    torch.cuda.set_stream(stream)
+
+    # algorithmic bytes of one launch: query rows, node records, PQ codes gathered, results
+    eng.search_device(dq, p, d_ids, d_dists, None, d_steps, d_nbrs, stream=stream.cuda_stream)
+    torch.cuda.synchronize()
+    eng.check_device_status()
+    info = eng.info
+    expansions = int(d_steps.sum().item())
+    gathered = int(d_nbrs.sum().item())
+    alg_bytes = nq * (4 * info.dim + 8 * k) + expansions * info.node_size + gathered * info.num_chunks
+
+    for _ in range(args.warmup):
+        eng.search_device(dq, p, d_ids, d_dists, stream=stream.cuda_stream)
+    barrier()
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+    with ClockSampler(local) as clk:
+        evs[0].record(stream)
+        for i in range(args.steps):
+            eng.search_device(dq, p, d_ids, d_dists, stream=stream.cuda_stream)
+            evs[i + 1].record(stream)
+        torch.cuda.synchronize()
+    clocks = clk.summary()
+    eng.check_device_status()
+    step_ms = [evs[i].elapsed_time(evs[i + 1]) for i in range(args.steps)]
+    total_ms = shard.reduce_max(evs[0].elapsed_time(evs[-1]), device=dev)
+    barrier()
+    value = world * args.steps * nq / (total_ms / 1000.0)
+
+    # per-query service latency at the same operating point
+    lat = eng.search_timed(q, p)[3]
+    p50, p99 = float(np.percentile(lat, 50)), float(np.percentile(lat, 99))
+
+    # end to end through the C ABI with pinned host buffers
+    hq = torch.from_numpy(q).pin_memory()
+    h_ids = torch.empty((nq, k), dtype=torch.int32).pin_memory()
+    h_dists = torch.empty((nq, k), dtype=torch.float32).pin_memory()
+    for _ in range(2):
+        eng.search_host_ptrs(hq.data_ptr(), nq, info.dim, p, h_ids.data_ptr(), h_dists.data_ptr())
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        eng.search_host_ptrs(hq.data_ptr(), nq, info.dim, p, h_ids.data_ptr(), h_dists.data_ptr())
+    e2e_s = shard.reduce_max(time.perf_counter() - t0, device=dev)
+    barrier()
+    step_recall = calc_recall(h_ids.numpy(), workloads.ground_truth(w, q, 10, device=f"cuda:{local}"), 10) \
+        if rank == 0 else None
+
+    if rank == 0:
+        peaks = read_peaks()
+        avg_ms = statistics.mean(step_ms)
+        achieved = alg_bytes / (avg_ms / 1000.0) / 1e9
+        traffic = read_profile_traffic(f"search_kernel_{w.name}.txt")
+        line = {
+            "metric": METRIC, "value": value, "unit": "queries/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded Gaussian mixture; SIFT/DEEP not present)",
+            "config": {"workload": workload_desc(w), "ef_search": ef, "recall_at_10": recall,
+                       "recall_at_10_step_batch": step_recall, "pipe_width": args.pipe_width,
+                       "early_exit": args.early_exit, "queries_per_step_per_gpu": nq,
+                       "l2": f"inputs larger than L2: page store {info.num_pages * 4096 / 1e6:.0f} MB + codes "
+                             f"{info.num_points * info.num_chunks / 1e6:.0f} MB vs 126 MB L2, no flush",
+                       "parallelism": f"query shards x{world}, index replicated"},
+            "recall_at_10": recall, "p50_ms": p50, "p99_ms": p99,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": achieved / peaks["hbm_gbs"], "peak_source": peaks["source"],
+                         "traffic": traffic, "algorithmic_bytes_per_launch": alg_bytes,
+                         "expansions_per_query": expansions / nq, "codes_per_query": gathered / nq},
+            "e2e": {"value": world * args.steps * nq / e2e_s, "unit": "queries/s",
+                    "h2d_bytes_per_step": int(q.nbytes), "d2h_bytes_per_step": int(nq * k * 8)},
+            "gpu_launches": args.steps,
+            "clocks": clocks,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(w, d, ef, args)
+        print(json.dumps(line), flush=True)
+    eng.close()
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -128,6 +128,11 @@ const char* qv_version(void);
 const char* qv_last_error(void);
 void qv_search_opts_default(qv_search_opts* opts);
 
+/* Parse and check an index directory on the host only (no GPU): discovery,
+ * disk-index header, PQ files, geometry.  The file-reading half of
+ * prepare_search_setup (bin/common/search_setup.hpp:73-119). */
+int qv_index_probe(const char* index_dir, int32_t data_type, qv_index_info* info);
+
 int qv_engine_create(const qv_engine_opts* opts, qv_engine** out);
 int qv_engine_create_from_arrays(const qv_index_arrays* arrays, int32_t device,
                                  int32_t page_store, qv_engine** out);
@@ -155,7 +160,8 @@ int qv_search_timed(qv_engine* engine, const float* queries, int64_t nq, int64_t
                     int32_t* found, float* query_ms, qv_search_stats* stats);
 
 /* Same search with DEVICE buffers on the engine's GPU, enqueued on `stream`
- * (a cudaStream_t; NULL = the engine's own stream) without a host
+ * (a cudaStream_t; NULL = the engine's own stream, cudaStreamLegacy for the
+ * legacy default stream) without a host
  * synchronisation.  steps [nq] (expansions) and nbrs [nq] (PQ codes
  * gathered) may be NULL.  Errors the kernel detects in the data are
  * reported by qv_check_device_status after the stream has drained. */

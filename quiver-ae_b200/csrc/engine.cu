@@ -392,6 +392,29 @@ void qv_search_opts_default(qv_search_opts* o) {
   o->lut_mode = QV_LUT_FP32;
 }
 
+int qv_index_probe(const char* index_dir, int32_t data_type, qv_index_info* info) {
+  return guarded([&] {
+    if (!index_dir || !info) fail(QV_ERR_INVALID_ARG, "null argument");
+    if (data_type != QV_UINT8 && data_type != QV_FLOAT && data_type != QV_INT8)
+      fail(QV_ERR_INVALID_ARG, "data_type must be QV_UINT8, QV_FLOAT or QV_INT8");
+    const std::string index_file = qv::find_index_file(index_dir);
+    const std::string prefix = qv::find_pq_prefix(index_dir);
+    const qv::Layout L = qv::parse_disk_index_header(index_file, data_type);
+    const qv::PQTables pq = qv::read_pq(prefix + "_pivots.bin", prefix + "_compressed.bin");
+    qv::check_layout(L, &pq);
+    info->num_points = L.num_points;
+    info->dim = L.dim;
+    info->max_degree = L.max_degree;
+    info->node_size = L.node_size;
+    info->data_size = L.data_size;
+    info->nodes_per_page = L.nodes_per_page;
+    info->num_pages = L.num_pages;
+    info->medoid = L.medoid;
+    info->data_type = data_type;
+    info->num_chunks = pq.num_chunks;
+  });
+}
+
 int qv_engine_create(const qv_engine_opts* opts, qv_engine** out) {
   return guarded([&] {
     if (!opts || !out || !opts->index_dir) fail(QV_ERR_INVALID_ARG, "null argument");

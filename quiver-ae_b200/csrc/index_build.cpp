@@ -247,6 +247,7 @@ struct Vamana {
           const auto& nl = newlist[b];
           degree[p] = static_cast<int32_t>(nl.size());
           std::copy(nl.begin(), nl.end(), graph.begin() + p * int64_t(R));
+          std::fill(graph.begin() + p * int64_t(R) + nl.size(), graph.begin() + (p + 1) * int64_t(R), -1);
           for (int32_t j : nl) rev.push_back({j, static_cast<int32_t>(p)});
         }
         std::sort(rev.begin(), rev.end());

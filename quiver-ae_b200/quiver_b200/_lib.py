@@ -70,6 +70,7 @@ ENGINE_SYMBOLS = {
     "qv_version": (C.c_char_p, []),
     "qv_last_error": (C.c_char_p, []),
     "qv_search_opts_default": (None, [C.POINTER(SearchOpts)]),
+    "qv_index_probe": (C.c_int, [C.c_char_p, C.c_int32, C.POINTER(IndexInfo)]),
     "qv_engine_create": (C.c_int, [C.POINTER(EngineOpts), C.POINTER(C.c_void_p)]),
     "qv_engine_create_from_arrays": (C.c_int, [C.POINTER(IndexArrays), C.c_int32, C.c_int32, C.POINTER(C.c_void_p)]),
     "qv_engine_info": (C.c_int, [C.c_void_p, C.POINTER(IndexInfo)]),

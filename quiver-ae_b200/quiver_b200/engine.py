@@ -134,6 +134,22 @@ class Engine:
             return ids, dists, found, st
         return ids, dists, found
 
+    def search_timed(self, queries: np.ndarray, params: SearchParams | None = None):
+        """qv_search_timed: also returns per-query service latency in ms."""
+        params = params or SearchParams()
+        q = np.ascontiguousarray(queries, dtype=np.float32)
+        nq, dim = q.shape
+        ids = np.empty((nq, params.topk), dtype=np.int32)
+        dists = np.empty((nq, params.topk), dtype=np.float32)
+        found = np.empty(nq, dtype=np.int32)
+        ms = np.empty(nq, dtype=np.float32)
+        st = _lib.SearchStats()
+        o = params.to_c()
+        _check(self._lib.qv_search_timed(self._h, C.c_void_p(q.ctypes.data), nq, dim, C.byref(o),
+                                         C.c_void_p(ids.ctypes.data), C.c_void_p(dists.ctypes.data),
+                                         C.c_void_p(found.ctypes.data), C.c_void_p(ms.ctypes.data), C.byref(st)))
+        return ids, dists, found, ms, st
+
     def search_host_ptrs(self, q_ptr: int, nq: int, dim: int, params: SearchParams, ids_ptr: int,
                          dists_ptr: int, found_ptr: int | None = None) -> None:
         """qv_search on raw host pointers (e.g. pinned torch tensors)."""
@@ -149,7 +165,9 @@ class Engine:
         def ptr(t):
             return C.c_void_p(t.data_ptr()) if t is not None else None
 
-        st = C.c_void_p(stream) if stream else None
+        # None: the engine's own stream; 0: the legacy default stream
+        # (cudaStreamLegacy, handle 0x1); anything else: that cudaStream_t.
+        st = None if stream is None else C.c_void_p(1 if stream == 0 else stream)
         _check(self._lib.qv_search_device(self._h, ptr(d_queries), d_queries.shape[0], C.byref(o), ptr(d_ids),
                                           ptr(d_dists), ptr(d_found), ptr(d_steps), ptr(d_nbrs), st))
 
