@@ -129,7 +129,12 @@ Plan make_plan(qv_engine* e, const qv_search_opts& o, int64_t nq) {
   const auto& L = e->L;
   pl.smax = L.max_degree <= 64 ? 2 : 4;
   pl.mc = e->M == 32 ? 32 : 0;
-  const int G = pl.smax <= 2 ? 4 : 2;
+  // --queries-per-block 0/1: one query per 128-thread CTA (the block kernel);
+  // Q >= 2: Q one-warp query slots per CTA (the warp kernel).  Both give
+  // identical results.
+  pl.block = o.queries_per_block <= 1;
+  const int rp = 32 * pl.smax;
+  const int G = pl.block ? qvk::kBlock / rp : (pl.smax <= 2 ? 4 : 2);
   int64_t off = 0;
   auto take = [&](int64_t bytes) {
     off = round_up(off, 16);
@@ -142,10 +147,22 @@ Plan make_plan(qv_engine* e, const qv_search_opts& o, int64_t nq) {
   y.off_q2 = take(L.dim * 4);
   y.off_lid = take(int64_t(o.ef_search) * 4);
   y.off_ldist = take(int64_t(o.ef_search) * 4);
-  y.off_nid = take(32 * pl.smax * 4);
-  y.off_ndist = take(32 * pl.smax * 4);
-  y.off_mid = take((int64_t(o.ef_search) + 32 * pl.smax) * 4);
-  y.off_mdist = take((int64_t(o.ef_search) + 32 * pl.smax) * 4);
+  if (pl.block) {
+    y.off_nid = take(int64_t(G) * rp * 4);
+    y.off_ndist = take(int64_t(G) * rp * 4);
+    y.off_spos = take(rp * 4);
+    y.off_sflag = take(rp * 4);
+    y.off_sorder = take(rp * 4);
+    y.off_S = take(rp * 4);
+    y.off_fpos = take(rp * 4);
+    y.off_fsrc = take(rp * 4);
+    y.off_misc = take(32 * 4);
+  } else {
+    y.off_nid = take(rp * 4);
+    y.off_ndist = take(rp * 4);
+    y.off_mid = take((int64_t(o.ef_search) + rp) * 4);
+    y.off_mdist = take((int64_t(o.ef_search) + rp) * 4);
+  }
   y.off_rid = take(int64_t(o.topk) * 4);
   y.off_rdist = take(int64_t(o.topk) * 4);
   y.rec_stride = static_cast<int32_t>(round_up(L.data_size, 16));
@@ -163,30 +180,24 @@ Plan make_plan(qv_engine* e, const qv_search_opts& o, int64_t nq) {
   }
   CK(cudaFuncSetAttribute(pl.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, e->max_smem_optin));
 
+  const int threads_per_slot = pl.block ? qvk::kBlock : 32;
   auto occupancy = [&](int slots) {
     int occ = 0;
     const int smem = slots * y.bytes;
     if (smem > e->max_smem_optin) return 0;
-    CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, pl.fn, slots * 32, smem));
+    CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, pl.fn, slots * threads_per_slot, smem));
     return occ;
   };
-  if (o.queries_per_block > 0) {
+  if (pl.block) {
+    pl.slots = 1;
+    pl.blocks_per_sm = occupancy(1);
+    if (pl.blocks_per_sm == 0) fail(QV_ERR_UNSUPPORTED, "a query slot does not fit in shared memory");
+  } else {
     pl.slots = o.queries_per_block;
     pl.blocks_per_sm = occupancy(pl.slots);
     if (pl.blocks_per_sm == 0)
       fail(QV_ERR_UNSUPPORTED, std::to_string(pl.slots) + " query slots of " + std::to_string(y.bytes) +
                                    " B do not fit in one CTA");
-  } else {
-    int best = 0;
-    for (int slots = 1; slots <= 8; ++slots) {
-      const int occ = occupancy(slots);
-      if (occ * slots >= best && occ > 0) {
-        best = occ * slots;
-        pl.slots = slots;
-        pl.blocks_per_sm = occ;
-      }
-    }
-    if (best == 0) fail(QV_ERR_UNSUPPORTED, "a query slot does not fit in shared memory");
   }
   pl.smem = pl.slots * y.bytes;
   const int64_t wave = int64_t(pl.blocks_per_sm) * e->num_sms;
@@ -194,6 +205,7 @@ Plan make_plan(qv_engine* e, const qv_search_opts& o, int64_t nq) {
   const int64_t needed = (nq + pl.slots - 1) / pl.slots;
   grid = std::max<int64_t>(1, std::min(grid, needed));
   pl.grid = static_cast<int>(grid);
+  pl.threads = pl.slots * threads_per_slot;
   return pl;
 }
 
@@ -240,7 +252,7 @@ qvk::SearchParams make_params(const qv_engine* e, const Plan& pl, const qv_searc
 
 void enqueue_search(qv_engine* e, const Plan& pl, const qvk::SearchParams& p, cudaStream_t st) {
   CK(cudaMemsetAsync(e->d_scratch, 0, 8 * sizeof(int32_t), st));
-  pl.launch(p, pl.grid, pl.slots * 32, pl.smem, st);
+  pl.launch(p, pl.grid, pl.threads, pl.smem, st);
   CK(cudaGetLastError());
 }
 

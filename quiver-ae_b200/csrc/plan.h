@@ -3,18 +3,21 @@
 
 #include <cuda_runtime.h>
 
+#include "search_block.cuh"
 #include "search_kernel.cuh"
 
 namespace qv {
 
 struct Plan {
   qvk::SlotLayout lay;
+  bool block = true;    // one 128-thread CTA per query; false: `slots` one-warp queries per CTA
   int smax = 2;         // neighbours per lane (R <= 32 * smax)
   int mc = 0;           // PQ code width the kernel is specialised for (0 = any)
   int slots = 1;        // query slots (warps) per CTA
   int blocks_per_sm = 0;
   int grid = 0;
   int smem = 0;
+  int threads = 0;      // CTA size
   const void* fn = nullptr;
   void (*launch)(const qvk::SearchParams&, int grid, int block, int smem, cudaStream_t) = nullptr;
 };
@@ -30,10 +33,20 @@ void launch_search(const qvk::SearchParams& p, int grid, int block, int smem, cu
   qvk::search_kernel<T, MC, SMAX><<<grid, block, smem, st>>>(p);
 }
 
+template <typename T, int MC, int RP>
+void launch_block(const qvk::SearchParams& p, int grid, int block, int smem, cudaStream_t st) {
+  qvk::search_block_kernel<T, MC, RP><<<grid, block, smem, st>>>(p);
+}
+
 template <typename T, int MC, int SMAX>
 void bind_one(Plan& pl) {
-  pl.fn = reinterpret_cast<const void*>(&qvk::search_kernel<T, MC, SMAX>);
-  pl.launch = &launch_search<T, MC, SMAX>;
+  if (pl.block) {
+    pl.fn = reinterpret_cast<const void*>(&qvk::search_block_kernel<T, MC, 32 * SMAX>);
+    pl.launch = &launch_block<T, MC, 32 * SMAX>;
+  } else {
+    pl.fn = reinterpret_cast<const void*>(&qvk::search_kernel<T, MC, SMAX>);
+    pl.launch = &launch_search<T, MC, SMAX>;
+  }
 }
 
 // PQ widths with a register-blocked code path; any other M uses MC = 0.

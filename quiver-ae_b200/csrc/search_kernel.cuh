@@ -52,6 +52,14 @@ struct SlotLayout {
   int32_t off_rec;               // kGroup record vectors
   int32_t rec_stride;            // bytes per staged vector, multiple of 16
   int32_t off_lane;              // int [W] pending node per pipe lane
+  // block kernel only
+  int32_t off_spos;              // int [32*SMAX] list insertion point of the u-th smallest new pair
+  int32_t off_sflag;             // int [32*SMAX] 1 if that pair is not already in the list
+  int32_t off_sorder;            // int [32*SMAX] slot of that pair in the unsorted new arrays
+  int32_t off_S;                 // int [32*SMAX] insertion points of the surviving pairs, ascending
+  int32_t off_fpos;              // int [32*SMAX] final list position of the j-th survivor
+  int32_t off_fsrc;              // int [32*SMAX] slot of the j-th survivor in the new arrays
+  int32_t off_misc;              // int [32] block scalars
 };
 
 struct SearchParams {
@@ -292,43 +300,43 @@ __device__ __forceinline__ int32_t select_warp(const Slot& s, int size, int lane
 
 // Insert (d, id) at the count of entries <= d, capping the size at k
 // (kernel_helpers.cuh:65-104; gpu_primitives.cuh:99-138 for k > 32).
-__device__ __forceinline__ int topk_insert_warp(const Slot& s, int fc, int k, float d,
+__device__ __forceinline__ int topk_insert_warp(int32_t* rid, float* rdist, int fc, int k, float d,
                                                 int32_t id, int lane) {
   const int nsz = fc < k ? fc + 1 : k;
   if (k <= 32) {
     const bool valid = lane < fc;
-    const float od = valid ? s.rdist[lane] : 0.f;
-    const int32_t oi = valid ? s.rid[lane] : 0;
+    const float od = valid ? rdist[lane] : 0.f;
+    const int32_t oi = valid ? rid[lane] : 0;
     const int pos = __popc(__ballot_sync(kFull, valid && od <= d));
     const float pd = __shfl_up_sync(kFull, od, 1);
     const int32_t pi = __shfl_up_sync(kFull, oi, 1);
     __syncwarp();
     if (lane < nsz) {
       if (lane == pos) {
-        s.rdist[lane] = d;
-        s.rid[lane] = id;
+        rdist[lane] = d;
+        rid[lane] = id;
       } else if (lane > pos) {
-        s.rdist[lane] = pd;
-        s.rid[lane] = pi;
+        rdist[lane] = pd;
+        rid[lane] = pi;
       }
     }
   } else {
     int pos = 0;
     for (int b = 0; b < fc; b += 32) {
       const int i = b + lane;
-      pos += __popc(__ballot_sync(kFull, i < fc && s.rdist[i] <= d));
+      pos += __popc(__ballot_sync(kFull, i < fc && rdist[i] <= d));
     }
     for (int b = ((nsz - 1) >> 5) << 5; b >= 0; b -= 32) {
       const int i = b + lane;
       const bool mv = i > pos && i < nsz;
       float v = 0.f;
       int32_t vi = 0;
-      if (mv) { v = s.rdist[i - 1]; vi = s.rid[i - 1]; }
+      if (mv) { v = rdist[i - 1]; vi = rid[i - 1]; }
       __syncwarp();
-      if (mv) { s.rdist[i] = v; s.rid[i] = vi; }
+      if (mv) { rdist[i] = v; rid[i] = vi; }
       __syncwarp();
     }
-    if (lane == 0) { s.rdist[pos] = d; s.rid[pos] = id; }
+    if (lane == 0) { rdist[pos] = d; rid[pos] = id; }
   }
   __syncwarp();
   return nsz;
@@ -518,7 +526,7 @@ __device__ int expand_lanes(const SearchParams& p, const Slot& s, QueryState& q,
         q.nbrs += deg[g];
         const float dx = exact_l2_warp<T>(s.q2, reinterpret_cast<const T*>(s.rec + g * p.lay.rec_stride),
                                           p.dim, lane);
-        if (q.fc < p.k || dx < s.rdist[p.k - 1]) q.fc = topk_insert_warp(s, q.fc, p.k, dx, node[g], lane);
+        if (q.fc < p.k || dx < s.rdist[p.k - 1]) q.fc = topk_insert_warp(s.rid, s.rdist, q.fc, p.k, dx, node[g], lane);
         int32_t next = select_warp(s, q.size, lane);
         q.step += 1;
         if (p.early_policy != 0 && gpruning_stop(p, s, q)) {

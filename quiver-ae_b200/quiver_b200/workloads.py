@@ -102,36 +102,40 @@ def ground_truth(w: Workload, q: np.ndarray, k: int = 10, device: str | None = N
 
 
 def _gt_torch(b: np.ndarray, q: np.ndarray, k: int, device: str) -> np.ndarray:
-    """Brute force on the GPU.  uint8 values are exact in bf16 and their
-    products accumulate exactly in fp32 (< 2^24), so ||x||^2 + ||q||^2 - 2 x.q
-    is the exact integer distance; float data uses fp32.  Ties at the k-th
-    place are broken by lower id within a base chunk."""
+    """Brute force on the GPU with an fp32 GEMM (TF32 off).  For uint8 data
+    every product and partial sum of x.q is an integer below 2^24, so the
+    distance ||x||^2 + ||q||^2 - 2 x.q is exact; float data is fp32.  Ties at
+    the k-th place are broken by lower id within a base chunk."""
     import torch
-    exact_int = b.dtype == np.uint8
-    dt = torch.bfloat16 if exact_int else torch.float32
-    out = np.empty((q.shape[0], k), dtype=np.int32)
-    bchunk = 1 << 18
-    qchunk = 2048
-    xs = []
-    for s in range(0, b.shape[0], bchunk):
-        x = torch.from_numpy(b[s:s + bchunk].astype(np.float32)).to(device)
-        xs.append((s, x.to(dt), (x * x).sum(1)))
-    for qs in range(0, q.shape[0], qchunk):
-        qb = torch.from_numpy(q[qs:qs + qchunk].astype(np.float32)).to(device)
-        qn = (qb * qb).sum(1, keepdim=True)
-        qd = qb.to(dt)
-        best_d = torch.full((qb.shape[0], k), float("inf"), device=device)
-        best_i = torch.zeros((qb.shape[0], k), dtype=torch.int64, device=device)
-        for s, xd, xn in xs:
-            dist = qn + xn[None, :] - 2 * torch.matmul(qd, xd.T).float()
-            td, ti = torch.topk(dist, min(k, dist.shape[1]), dim=1, largest=False, sorted=True)
-            cand_d = torch.cat([best_d, td], 1)
-            cand_i = torch.cat([best_i, ti + s], 1)
-            order = torch.argsort(cand_i, dim=1)
-            cand_d = torch.gather(cand_d, 1, order)
-            cand_i = torch.gather(cand_i, 1, order)
-            sd, si = torch.sort(cand_d, dim=1, stable=True)
-            best_d = sd[:, :k]
-            best_i = torch.gather(cand_i, 1, si[:, :k])
-        out[qs:qs + qb.shape[0]] = best_i.to(torch.int32).cpu().numpy()
-    return out
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        out = np.empty((q.shape[0], k), dtype=np.int32)
+        bchunk = 1 << 18
+        qchunk = 2048
+        xs = []
+        for s in range(0, b.shape[0], bchunk):
+            x = torch.from_numpy(b[s:s + bchunk].astype(np.float32)).to(device)
+            xs.append((s, x, (x * x).sum(1)))
+        for qs in range(0, q.shape[0], qchunk):
+            qb = torch.from_numpy(q[qs:qs + qchunk].astype(np.float32)).to(device)
+            qn = (qb * qb).sum(1, keepdim=True)
+            best_d = torch.full((qb.shape[0], k), float("inf"), device=device)
+            best_i = torch.zeros((qb.shape[0], k), dtype=torch.int64, device=device)
+            for s, x, xn in xs:
+                dot = torch.matmul(qb, x.T)
+                assert dot.dtype == torch.float32
+                dist = qn + xn[None, :] - 2 * dot
+                td, ti = torch.topk(dist, min(k, dist.shape[1]), dim=1, largest=False, sorted=True)
+                cand_d = torch.cat([best_d, td], 1)
+                cand_i = torch.cat([best_i, ti + s], 1)
+                order = torch.argsort(cand_i, dim=1)
+                cand_d = torch.gather(cand_d, 1, order)
+                cand_i = torch.gather(cand_i, 1, order)
+                sd, si = torch.sort(cand_d, dim=1, stable=True)
+                best_d = sd[:, :k]
+                best_i = torch.gather(cand_i, 1, si[:, :k])
+            out[qs:qs + qb.shape[0]] = best_i.to(torch.int32).cpu().numpy()
+        return out
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev

@@ -47,3 +47,18 @@ def test_lut_adc_l2_bit_exact(request, fixture):
         ref_lut, ref_q2 = pyoracle.build_lut(ix, q[qof[j]])
         assert np.float32(adc_h[j]).view(np.uint32) == np.float32(pyoracle.adc(ref_lut, ix.codes[ids[j]])).view(np.uint32)
         assert np.float32(l2_h[j]).view(np.uint32) == np.float32(pyoracle.exact_l2(ix, ref_q2, int(ids[j]))).view(np.uint32)
+
+
+@pytest.mark.parametrize("dtype,dim", [("uint8", 128), ("float", 96)])
+def test_gpu_ground_truth_is_exact(dtype, dim):
+    """The GPU brute force behind the benchmark's recall equals the exact host one."""
+    from quiver_b200 import builder, workloads
+    base = builder.synth_mixture(9, 300_000, dim, 30, 20.0 if dtype == "uint8" else 0.1, dtype)
+    q = builder.synth_mixture(9, 64, dim, 30, 20.0 if dtype == "uint8" else 0.1, dtype, stream=1)
+    ref, ref_d = builder.ground_truth(base, q, 10)
+    got = workloads._gt_torch(base, q, 10, "cuda:0")
+    exact = ((base[got].astype(np.float64) - q[:, None, :].astype(np.float64)) ** 2).sum(-1)
+    if dtype == "uint8":  # integer distances: equal up to the choice among tied ids
+        np.testing.assert_array_equal(np.sort(exact, axis=1), ref_d.astype(np.float64))
+    else:  # fp32 GEMM vs double accumulation: the same set up to near-ties
+        assert np.mean([len(set(a) & set(b)) for a, b in zip(got, ref)]) >= 9.9
