@@ -184,25 +184,42 @@ __device__ __forceinline__ void merge_visit_select(const SearchParams& p, const 
   const int node = s.misc[kMiscNode + gg];
   const float* nd = s.nd + gg * RP;
   const uint32_t* ni = s.ni + gg * RP;
-  // M1: rank among the new pairs, insertion point in the list, duplicate test
-  if (tid < deg) {
+  // M1: the new pairs arrive as RP / 32 sorted runs of 32 (sorted per warp
+  // after the ADC).  A pair's rank among them is its index in its run plus,
+  // for every other run, the pairs below it (pairs of lower runs win ties,
+  // so the ranks are a permutation).  A pair whose id repeats an earlier
+  // pair's (an adjacency list that repeats an id) is dropped like one whose
+  // id is already in the list: the reference's compaction keeps one of
+  // adjacent equal ids.
+  if (tid < RP) {
     const float kd = nd[tid];
     const uint32_t ki = ni[tid];
-    // ranks form a permutation; of several pairs with one id (an adjacency
-    // list that repeats an id) only the first survives, as the reference's
-    // compaction keeps one of adjacent equal ids
-    int rnew = 0, twin = 0;
-    for (int u = 0; u < deg; ++u) {
-      const bool lt = key_less(nd[u], ni[u], kd, ki);
-      const bool eq = !lt && !key_less(kd, ki, nd[u], ni[u]);
-      rnew += (lt || (eq && u < tid)) ? 1 : 0;
-      twin += (eq && u < tid) ? 1 : 0;
+    if (ki != 0xffffffffu) {
+      const int run = tid >> 5, i = tid & 31;
+      const float* rd = nd + (run << 5);
+      const uint32_t* ri = ni + (run << 5);
+      int rnew = i;
+      bool twin = i > 0 && ((ri[i - 1] ^ ki) & kIdMask) == 0 && rd[i - 1] == kd;
+#pragma unroll
+      for (int o = 0; o < RP / 32; ++o) {
+        if (o == run) continue;
+        const float* od = nd + (o << 5);
+        const uint32_t* oi = ni + (o << 5);
+        const int lb = lower_bound_s(od, oi, 32, kd, ki);
+        if (o < run) {
+          const bool eq = lb < 32 && od[lb] == kd && ((oi[lb] ^ ki) & kIdMask) == 0;
+          rnew += lb + (eq ? 1 : 0);
+          twin = twin || eq;
+        } else {
+          rnew += lb;
+        }
+      }
+      const int r = lower_bound_s(s.ldist, s.lid, sz, kd, ki);
+      const bool dup = twin || (r < sz && ((s.lid[r] ^ ki) & kIdMask) == 0);
+      s.spos[rnew] = r;
+      s.sflag[rnew] = dup ? 0 : 1;
+      s.sorder[rnew] = tid;
     }
-    const int r = lower_bound_s(s.ldist, s.lid, sz, kd, ki);
-    const bool dup = twin > 0 || (r < sz && ((s.lid[r] ^ ki) & kIdMask) == 0);
-    s.spos[rnew] = r;
-    s.sflag[rnew] = dup ? 0 : 1;
-    s.sorder[rnew] = tid;
   }
   if (warp == 3) {  // visit: exact distance of the expanded node into the top-k
     const float dx = exact_l2_warp<T>(s.q2, reinterpret_cast<const T*>(s.rec + gg * p.lay.rec_stride), p.dim,
@@ -366,9 +383,12 @@ __device__ int expand_block(const SearchParams& p, const BSlot& s, uint32_t mask
         d = acc;
       }
     }
-    if (g < G) {
-      s.nd[g * RP + e] = d;
-      s.ni[g * RP + e] = live ? nb : 0xffffffffu;
+    {  // each warp sorts its 32 pairs; padding (inf, 0xffffffff) sorts last
+      float kd[1] = {d};
+      uint32_t ki[1] = {live ? nb : 0xffffffffu};
+      bitonic_sort<1>(kd, ki, tid & 31);
+      s.nd[g * RP + e] = kd[0];
+      s.ni[g * RP + e] = ki[0];
     }
     __syncthreads();
     if (s.misc[kMiscErr]) return s.misc[kMiscErr];
