@@ -6,20 +6,24 @@
 // work of a hop is spread over four warps:
 //   fetch + ADC   one neighbour per thread; a group of 128 / RP pipe lanes
 //                 (RP = R rounded up to 64 or 128) is fetched and scored at
-//                 once, so their node-record and code gathers overlap;
-//   merge         every new pair finds its rank among the new pairs and its
-//                 insertion point in the list (binary search); pairs already
-//                 in the list are dropped (kernel_helpers.cuh:331-335 places
-//                 them right after their twin and :440-455 removes them);
-//                 the survivors' final positions come from a block prefix
-//                 count; the list then shifts in place from the first
-//                 insertion point, highest chunk first, and the survivors
-//                 drop into the gaps; entries pushed past ef are discarded;
-//   visit         warp 3 scores the expanded node exactly and updates the
-//                 top-k while the other warps merge;
-//   select        warp 0 scans for the first unvisited entry starting from
-//                 a lower bound that the merge keeps up to date, instead of
-//                 from index 0.
+//                 once, so their node-record and code gathers overlap; each
+//                 warp sorts its 32 pairs, and the runs of a record are
+//                 merged by binary search into one sorted array per record;
+//   merge         per record, in lane order: every new pair binary-searches
+//                 its insertion point in the list; a pair whose id is in the
+//                 list or repeats an earlier pair's id is dropped
+//                 (kernel_helpers.cuh:331-335 places it right after its twin
+//                 and :440-455 removes it); survivors get their final
+//                 positions from a block prefix count; old entries move up by
+//                 the survivors inserted before them; entries pushed past ef
+//                 are discarded;
+//   visit         warp 3 scores the expanded node exactly, updates the top-k
+//                 and runs gpruning while the other warps search;
+//   select        the first unvisited entry of the merged list is either the
+//                 first survivor or the first unvisited old entry at or after
+//                 a lower bound (all entries before it are visited), so it is
+//                 known before the merged list is written: its writer sets the
+//                 visited bit.  Three barriers per expanded node.
 #pragma once
 
 #include "search_kernel.cuh"
@@ -27,6 +31,8 @@
 namespace qvk {
 
 constexpr int kBlock = 128;
+constexpr int kGpThread = 96;     // warp 3, lane 0: gpruning state and counters
+constexpr int kFastEntries = 4;   // list entries per thread held in registers (ef <= 512)
 
 // block scalars (misc[])
 enum : int {
@@ -40,6 +46,7 @@ enum : int {
   kMiscDeg = 12,    // [4] degree of each record of the group
   kMiscNode = 16,   // [4] node of each record of the group
   kMiscWs = 20,     // [4] lane of each record of the group
+  kMiscFu = 24,     // [4] per-warp first unvisited old entry at or after the hint
 };
 
 struct BSlot {
@@ -47,14 +54,12 @@ struct BSlot {
   float* q2;
   uint32_t* lid;
   float* ldist;
-  float* nd;        // [G * RP] new pair distances, slot order
-  uint32_t* ni;     // [G * RP] new pair ids
-  int* spos;
-  int* sflag;
-  int* sorder;
-  int* S;
-  int* fpos;
-  int* fsrc;
+  float* nd;        // [G * RP] new pairs, per-warp sorted runs
+  uint32_t* ni;
+  float* sd;        // [G * RP] new pairs of each record in key order
+  uint32_t* si;
+  int* S;           // [RP] insertion points of the survivors, ascending
+  int* fsrc;        // [RP] index in sd/si of the j-th survivor
   int32_t* rid;
   float* rdist;
   uint8_t* rec;
@@ -70,11 +75,9 @@ __device__ __forceinline__ BSlot make_bslot(uint8_t* base, const SlotLayout& L) 
   s.ldist = reinterpret_cast<float*>(base + L.off_ldist);
   s.nd = reinterpret_cast<float*>(base + L.off_ndist);
   s.ni = reinterpret_cast<uint32_t*>(base + L.off_nid);
-  s.spos = reinterpret_cast<int*>(base + L.off_spos);
-  s.sflag = reinterpret_cast<int*>(base + L.off_sflag);
-  s.sorder = reinterpret_cast<int*>(base + L.off_sorder);
+  s.sd = reinterpret_cast<float*>(base + L.off_spos);
+  s.si = reinterpret_cast<uint32_t*>(base + L.off_sflag);
   s.S = reinterpret_cast<int*>(base + L.off_S);
-  s.fpos = reinterpret_cast<int*>(base + L.off_fpos);
   s.fsrc = reinterpret_cast<int*>(base + L.off_fsrc);
   s.rid = reinterpret_cast<int32_t*>(base + L.off_rid);
   s.rdist = reinterpret_cast<float*>(base + L.off_rdist);
@@ -138,7 +141,7 @@ __device__ __forceinline__ void build_lut_block(const SearchParams& p, const flo
   __syncthreads();
 }
 
-// Per-query state that only thread 0 needs (gpruning, counters).
+// Per-query state that only kGpThread keeps (gpruning, counters).
 struct BlockQuery {
   int step, cnt, last_fc;
   float last_top1, last_topk;
@@ -146,8 +149,8 @@ struct BlockQuery {
 };
 
 // Warp 0: first unvisited entry at or after the hint; marks it, advances the
-// hint and stores the result in lane[w].  Returns the node (warp-uniform).
-__device__ __forceinline__ int32_t select_block_warp(const BSlot& s, int w, int lane) {
+// hint and stores the result in lane[w] (-1 instead when the query stopped).
+__device__ __forceinline__ void select_block_warp(const BSlot& s, int w, int lane) {
   const int size = s.misc[kMiscSize];
   const int h = s.misc[kMiscHint];
   int32_t next = -1;
@@ -167,157 +170,190 @@ __device__ __forceinline__ int32_t select_block_warp(const BSlot& s, int w, int 
       break;
     }
   }
-  if (next == -1 && lane == 0) s.misc[kMiscHint] = size;
-  if (lane == 0) s.lane[w] = next;
+  if (lane == 0) {
+    if (next == -1) s.misc[kMiscHint] = size;
+    s.lane[w] = s.misc[kMiscStop] ? -1 : next;
+  }
   __syncwarp();
-  return next;
 }
 
-// Merge record gg of the current group into the list, visit its node on
-// warp 3, then select the lane's next node and test gpruning on warp 0.
+// Warp 3: exact distance of the expanded node into the top-k, then the step
+// count and gpruning (kernel_q1.cuh:524-545) on lane 0.
+template <typename T>
+__device__ __forceinline__ void visit_warp(const SearchParams& p, const BSlot& s, int gg, int node, int deg,
+                                           BlockQuery& bq, int lane) {
+  const float dx = exact_l2_warp<T>(s.q2, reinterpret_cast<const T*>(s.rec + gg * p.lay.rec_stride), p.dim, lane);
+  int fc = s.misc[kMiscFc];
+  if (fc < p.k || dx < s.rdist[p.k - 1]) {
+    fc = topk_insert_warp(s.rid, s.rdist, fc, p.k, dx, node, lane);
+    if (lane == 0) s.misc[kMiscFc] = fc;
+  }
+  if (lane == 0) {
+    bq.step += 1;
+    bq.nbrs += deg;
+    if (p.early_policy != 0) {
+      const float top1 = s.rdist[0];
+      const float topk = s.rdist[p.k - 1];
+      const bool improved = fc > bq.last_fc || top1 < bq.last_top1 || topk < bq.last_topk;
+      if (bq.step < p.gp_warmup)
+        bq.cnt = 0;
+      else
+        bq.cnt = improved ? 0 : bq.cnt + 1;
+      bq.last_fc = fc;
+      bq.last_top1 = top1;
+      bq.last_topk = topk;
+      if (p.early_policy == 2 && bq.step >= p.gp_warmup && p.gp_patience > 0 && bq.cnt >= p.gp_patience)
+        s.misc[kMiscStop] = 1;
+    }
+  }
+}
+
+// Merge record gg of the current group into the list, visit its node, and
+// select the lane's next node.
 template <typename T, int RP>
 __device__ __forceinline__ void merge_visit_select(const SearchParams& p, const BSlot& s, int gg,
                                                    BlockQuery& bq) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int sz = s.misc[kMiscSize];
+  const int h = s.misc[kMiscHint];
   const int deg = s.misc[kMiscDeg + gg];
   const int node = s.misc[kMiscNode + gg];
-  const float* nd = s.nd + gg * RP;
-  const uint32_t* ni = s.ni + gg * RP;
-  // M1: the new pairs arrive as RP / 32 sorted runs of 32 (sorted per warp
-  // after the ADC).  A pair's rank among them is its index in its run plus,
-  // for every other run, the pairs below it (pairs of lower runs win ties,
-  // so the ranks are a permutation).  A pair whose id repeats an earlier
-  // pair's (an adjacency list that repeats an id) is dropped like one whose
-  // id is already in the list: the reference's compaction keeps one of
-  // adjacent equal ids.
-  if (tid < RP) {
-    const float kd = nd[tid];
-    const uint32_t ki = ni[tid];
-    if (ki != 0xffffffffu) {
-      const int run = tid >> 5, i = tid & 31;
-      const float* rd = nd + (run << 5);
-      const uint32_t* ri = ni + (run << 5);
-      int rnew = i;
-      bool twin = i > 0 && ((ri[i - 1] ^ ki) & kIdMask) == 0 && rd[i - 1] == kd;
-#pragma unroll
-      for (int o = 0; o < RP / 32; ++o) {
-        if (o == run) continue;
-        const float* od = nd + (o << 5);
-        const uint32_t* oi = ni + (o << 5);
-        const int lb = lower_bound_s(od, oi, 32, kd, ki);
-        if (o < run) {
-          const bool eq = lb < 32 && od[lb] == kd && ((oi[lb] ^ ki) & kIdMask) == 0;
-          rnew += lb + (eq ? 1 : 0);
-          twin = twin || eq;
-        } else {
-          rnew += lb;
-        }
-      }
-      const int r = lower_bound_s(s.ldist, s.lid, sz, kd, ki);
-      const bool dup = twin || (r < sz && ((s.lid[r] ^ ki) & kIdMask) == 0);
-      s.spos[rnew] = r;
-      s.sflag[rnew] = dup ? 0 : 1;
-      s.sorder[rnew] = tid;
-    }
+  const int w = s.misc[kMiscWs + gg];
+  const float* sd = s.sd + gg * RP;
+  const uint32_t* si = s.si + gg * RP;
+  const bool fast = sz <= kBlock * kFastEntries;
+
+  // Phase A: insertion points, survivors, reads of the old entries, visit.
+  bool surv = false;
+  int r = 0;
+  if (tid < deg) {
+    const float kd = sd[tid];
+    const uint32_t ki = si[tid];
+    const bool twin = tid > 0 && si[tid - 1] == ki;
+    r = lower_bound_s(s.ldist, s.lid, sz, kd, ki);
+    surv = !twin && !(r < sz && ((s.lid[r] ^ ki) & kIdMask) == 0);
   }
-  if (warp == 3) {  // visit: exact distance of the expanded node into the top-k
-    const float dx = exact_l2_warp<T>(s.q2, reinterpret_cast<const T*>(s.rec + gg * p.lay.rec_stride), p.dim,
-                                      lane);
-    const int fc = s.misc[kMiscFc];
-    if (fc < p.k || dx < s.rdist[p.k - 1]) {
-      const int nfc = topk_insert_warp(s.rid, s.rdist, fc, p.k, dx, node, lane);
-      if (lane == 0) s.misc[kMiscFc] = nfc;
-    }
-  }
-  __syncthreads();
-  // M2: survivors in key order get ranks by a block prefix count
-  const int surv = (tid < deg) ? s.sflag[tid] : 0;
   const unsigned bal = __ballot_sync(kFull, surv);
-  if (lane == 0) s.misc[kMiscWtot + warp] = __popc(bal);
-  __syncthreads();
-  int before = 0, nsurv = 0;
+  uint32_t vid[kFastEntries];
+  float vd[kFastEntries];
+  int fu = 0x7fffffff;
+  if (fast) {
 #pragma unroll
-  for (int w = 0; w < 4; ++w) {
-    const int t = s.misc[kMiscWtot + w];
-    before += (w < warp) ? t : 0;
+    for (int e = 0; e < kFastEntries; ++e) {
+      const int i = tid + kBlock * e;
+      vid[e] = 0;
+      vd[e] = 0.f;
+      if (i < sz) {
+        vid[e] = s.lid[i];
+        vd[e] = s.ldist[i];
+        if (i >= h && (vid[e] & kVisited) == 0) fu = min(fu, i);
+      }
+    }
+    fu = __reduce_min_sync(kFull, fu);
+  }
+  if (lane == 0) {
+    s.misc[kMiscWtot + warp] = __popc(bal);
+    s.misc[kMiscFu + warp] = fu;
+  }
+  if (warp == 3) visit_warp<T>(p, s, gg, node, deg, bq, lane);
+  __syncthreads();
+
+  // Phase B: survivor ranks by a block prefix count.
+  int before = 0, nsurv = 0;
+  fu = 0x7fffffff;
+#pragma unroll
+  for (int x = 0; x < 4; ++x) {
+    const int t = s.misc[kMiscWtot + x];
+    before += (x < warp) ? t : 0;
     nsurv += t;
+    fu = min(fu, s.misc[kMiscFu + x]);
   }
   if (surv) {
     const int j = before + __popc(bal & ((1u << lane) - 1u));
-    s.S[j] = s.spos[tid];
-    s.fpos[j] = s.spos[tid] + j;
-    s.fsrc[j] = s.sorder[tid];
+    s.S[j] = r;
+    s.fsrc[j] = tid;
   }
   __syncthreads();
-  // M3: shift the list in place from the first insertion point, high chunks first
+
+  const int nsize = min(sz + nsurv, p.ef);
+  const bool stopped = s.misc[kMiscStop] != 0;
+  if (fast) {
+    // Phase C: shifted writes; the writer of the first unvisited entry marks it.
+    const int first = nsurv > 0 ? s.S[0] : 0x7fffffff;
+    int sel = 0x7fffffff;
+    if (nsurv > 0) sel = first;  // survivor 0 lands at S[0] + 0
+    if (fu != 0x7fffffff) sel = min(sel, fu + count_le(s.S, nsurv, fu));
+    if (sel >= nsize) sel = -1;
+#pragma unroll
+    for (int e = 0; e < kFastEntries; ++e) {
+      const int i = tid + kBlock * e;
+      if (i < sz) {
+        const int dst = i >= first ? i + count_le(s.S, nsurv, i) : i;
+        const bool mark = dst == sel;
+        if (dst < p.ef && (dst != i || mark)) {
+          s.lid[dst] = vid[e] | (mark ? kVisited : 0u);
+          s.ldist[dst] = vd[e];
+        }
+        if (mark && !stopped) s.lane[w] = static_cast<int32_t>(vid[e] & kIdMask);
+      }
+    }
+    if (tid < nsurv) {
+      const int fp = s.S[tid] + tid;
+      if (fp < p.ef) {
+        const int src = s.fsrc[tid];
+        const bool mark = fp == sel;
+        s.lid[fp] = si[src] | (mark ? kVisited : 0u);
+        s.ldist[fp] = sd[src];
+        if (mark && !stopped) s.lane[w] = static_cast<int32_t>(si[src]);
+      }
+    }
+    if (tid == 0) {
+      s.misc[kMiscSize] = nsize;
+      s.misc[kMiscHint] = sel >= 0 ? sel + 1 : nsize;
+      if (sel < 0 || stopped) s.lane[w] = -1;
+    }
+    __syncthreads();
+    return;
+  }
+
+  // Long lists (ef > 512): shift in 128-entry chunks, highest first, then scan.
   if (nsurv > 0) {
     const int first = s.S[0];
     if (first < sz) {
       for (int cb = ((sz - 1) / kBlock) * kBlock; cb >= (first / kBlock) * kBlock; cb -= kBlock) {
         const int i = cb + tid;
         const bool mv = i >= first && i < sz;
-        uint32_t vid = 0;
-        float vd = 0.f;
+        uint32_t xid = 0;
+        float xd = 0.f;
         int dst = 0;
         if (mv) {
-          vid = s.lid[i];
-          vd = s.ldist[i];
+          xid = s.lid[i];
+          xd = s.ldist[i];
           dst = i + count_le(s.S, nsurv, i);
         }
         __syncthreads();
         if (mv && dst < p.ef) {
-          s.lid[dst] = vid;
-          s.ldist[dst] = vd;
+          s.lid[dst] = xid;
+          s.ldist[dst] = xd;
         }
         __syncthreads();
       }
     }
-    // M4: survivors into the gaps
     if (tid < nsurv) {
-      const int fp = s.fpos[tid];
+      const int fp = s.S[tid] + tid;
       if (fp < p.ef) {
         const int src = s.fsrc[tid];
-        s.lid[fp] = ni[src];
-        s.ldist[fp] = nd[src];
+        s.lid[fp] = si[src];
+        s.ldist[fp] = sd[src];
       }
     }
     if (tid == 0) {
-      const int nsize = min(sz + nsurv, p.ef);
-      const int h = s.misc[kMiscHint];
-      const int nh = min(h + count_le(s.S, nsurv, h), s.S[0]);
       s.misc[kMiscSize] = nsize;
-      s.misc[kMiscHint] = min(nh, nsize);
+      s.misc[kMiscHint] = min(min(h + count_le(s.S, nsurv, h), first), nsize);
     }
     __syncthreads();
   }
-  // select + gpruning
-  if (warp == 0) {
-    const int w = s.misc[kMiscWs + gg];
-    int32_t next = select_block_warp(s, w, lane);
-    if (lane == 0) {
-      bq.step += 1;
-      bq.nbrs += deg;
-      if (p.early_policy != 0) {
-        const int fc = s.misc[kMiscFc];
-        const float top1 = s.rdist[0];
-        const float topk = s.rdist[p.k - 1];
-        const bool improved = fc > bq.last_fc || top1 < bq.last_top1 || topk < bq.last_topk;
-        if (bq.step < p.gp_warmup)
-          bq.cnt = 0;
-        else
-          bq.cnt = improved ? 0 : bq.cnt + 1;
-        bq.last_fc = fc;
-        bq.last_top1 = top1;
-        bq.last_topk = topk;
-        if (p.early_policy == 2 && bq.step >= p.gp_warmup && p.gp_patience > 0 && bq.cnt >= p.gp_patience) {
-          s.misc[kMiscStop] = 1;
-          s.lane[w] = -1;
-        }
-      }
-    }
-    (void)next;
-  }
+  if (warp == 0) select_block_warp(s, w, lane);
   __syncthreads();
 }
 
@@ -387,11 +423,32 @@ __device__ int expand_block(const SearchParams& p, const BSlot& s, uint32_t mask
       float kd[1] = {d};
       uint32_t ki[1] = {live ? nb : 0xffffffffu};
       bitonic_sort<1>(kd, ki, tid & 31);
-      s.nd[g * RP + e] = kd[0];
-      s.ni[g * RP + e] = ki[0];
+      s.nd[tid] = kd[0];
+      s.ni[tid] = ki[0];
     }
     __syncthreads();
     if (s.misc[kMiscErr]) return s.misc[kMiscErr];
+    {  // merge the runs of each record into key order: rank = index in run +
+       // pairs below it in the other runs (lower runs win ties)
+      const float kd = s.nd[tid];
+      const uint32_t ki = s.ni[tid];
+      if (ki != 0xffffffffu) {
+        const int run = e >> 5, i = e & 31;
+        int rank = i;
+#pragma unroll
+        for (int o = 0; o < RP / 32; ++o) {
+          if (o == run) continue;
+          const float* od = s.nd + g * RP + (o << 5);
+          const uint32_t* oi = s.ni + g * RP + (o << 5);
+          const int lb = lower_bound_s(od, oi, 32, kd, ki);
+          const bool eq = o < run && lb < 32 && od[lb] == kd && ((oi[lb] ^ ki) & kIdMask) == 0;
+          rank += lb + (eq ? 1 : 0);
+        }
+        s.sd[g * RP + rank] = kd;
+        s.si[g * RP + rank] = ki;
+      }
+    }
+    __syncthreads();
     for (int gg = 0; gg < gact; ++gg) merge_visit_select<T, RP>(p, s, gg, bq);
   }
   return 0;
@@ -425,6 +482,8 @@ __device__ void run_query_block(const SearchParams& p, const BSlot& s, int64_t q
 
   int err = expand_block<T, MC, RP>(p, s, 1u, qid, bq);  // boot: the entry on lane 0
   if (!err) {
+    // lanes 1..W-1 are seeded whether or not the boot hop stopped the query
+    // (kernel_q1.cuh:367-371); their picks matter only when it did not
     if (warp == 0)
       for (int w = 1; w < p.W; ++w) select_block_warp(s, w, lane);
     __syncthreads();
@@ -435,7 +494,7 @@ __device__ void run_query_block(const SearchParams& p, const BSlot& s, int64_t q
         if (s.lane[w] != -1) active |= 1u << w;
       if (!active) break;
       if (++iters > p.max_iters) {
-        if (tid == 0) report_error(p, kErrHopCap, qid, bq.step, 0);
+        if (tid == 0) report_error(p, kErrHopCap, qid, iters, 0);
         err = kErrHopCap;
         break;
       }
@@ -452,7 +511,7 @@ __device__ void run_query_block(const SearchParams& p, const BSlot& s, int64_t q
     p.out_ids[qid * p.k + i] = s.rid[i];
     p.out_dists[qid * p.k + i] = s.rdist[i];
   }
-  if (tid == 0) {
+  if (tid == kGpThread) {
     if (p.out_found) p.out_found[qid] = err ? -1 : s.misc[kMiscFc];
     if (p.out_steps) p.out_steps[qid] = bq.step;
     if (p.out_nbrs) p.out_nbrs[qid] = bq.nbrs;

@@ -53,12 +53,10 @@ struct SlotLayout {
   int32_t rec_stride;            // bytes per staged vector, multiple of 16
   int32_t off_lane;              // int [W] pending node per pipe lane
   // block kernel only
-  int32_t off_spos;              // int [32*SMAX] list insertion point of the u-th smallest new pair
-  int32_t off_sflag;             // int [32*SMAX] 1 if that pair is not already in the list
-  int32_t off_sorder;            // int [32*SMAX] slot of that pair in the unsorted new arrays
-  int32_t off_S;                 // int [32*SMAX] insertion points of the surviving pairs, ascending
-  int32_t off_fpos;              // int [32*SMAX] final list position of the j-th survivor
-  int32_t off_fsrc;              // int [32*SMAX] slot of the j-th survivor in the new arrays
+  int32_t off_spos;              // float [G*RP] new pairs of each record in key order (distances)
+  int32_t off_sflag;             // uint [G*RP]   (ids)
+  int32_t off_S;                 // int [RP] insertion points of the surviving pairs, ascending
+  int32_t off_fsrc;              // int [RP] key-order index of the j-th survivor
   int32_t off_misc;              // int [32] block scalars
 };
 
