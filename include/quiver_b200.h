@@ -171,6 +171,26 @@ int qv_search_device(qv_engine* engine, const float* d_queries, int64_t nq,
                      void* stream);
 int qv_check_device_status(qv_engine* engine);
 
+/* Search with HOST buffers that allocates no device memory -- for callers
+ * that may not call cudaMalloc once their index is loaded (a plugin whose
+ * host application owns the device allocator, a serving loop that cannot
+ * take an allocation's implicit synchronisation or its failure under memory
+ * pressure).  This entry point has no counterpart in the reference.  The
+ * search kernel's scratch -- work counter, error words and device copies of
+ * the queries and results -- is a file-scope device array of
+ * QV_NOALLOC_SCRATCH_BYTES held by every GPU that loads the library, so a
+ * call may carry at most
+ *   256 + align256(nq*dim*4) + 2*align256(nq*topk*4) + align256(nq*4)
+ * bytes (about 7,000 queries of 128 dims at top-10); larger batches are
+ * rejected with QV_ERR_INVALID_ARG.  The first call on a device looks up the
+ * array's address with that device current; make it before any stream
+ * capture.  Calls share the array: calls that overlap on the GPU race and
+ * must be serialised by the caller.  Results equal qv_search's. */
+#define QV_NOALLOC_SCRATCH_BYTES (4u << 20)
+int qv_search_noalloc(qv_engine* engine, const float* queries, int64_t nq, int64_t dim,
+                      const qv_search_opts* opts, int32_t* ids, float* dists,
+                      int32_t* found);
+
 /* Launch geometry qv_search_device would use (grid, slots, smem). */
 int qv_plan(qv_engine* engine, const qv_search_opts* opts, int64_t nq,
             qv_search_stats* plan);

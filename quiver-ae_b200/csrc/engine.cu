@@ -14,6 +14,7 @@
 #include <cstdio>
 #include <cstring>
 #include <memory>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -628,6 +629,98 @@ int qv_check_device_status(qv_engine* e) {
   });
 }
 
+
+// ---------------------------------------------------- scratch-free search --
+//
+// qv_search_noalloc serves callers that may not allocate device memory on
+// their search path: plugins whose host application owns the device
+// allocator and forbids them from calling cudaMalloc, and serving loops
+// where a cudaMalloc (with its implicit device synchronisation) or a failed
+// allocation under memory pressure is not acceptable once the index is
+// loaded.  The search kernel's scratch -- its work counter, its error words
+// and the device copies of the queries and results -- lives in the
+// file-scope array below instead of engine-owned allocations.  The array
+// is 4 MiB; every GPU that loads this library holds it until the process
+// exits.  Its device address is looked up once per device, by the first
+// call on that device with that device current; make that first call
+// before any stream capture.  All calls share the array and it keeps the
+// last call's contents; the work counter and error words are cleared at the
+// start of every call.  Calls that overlap on the GPU (two host threads, or
+// two engines on one device) race on the array and must be serialised by
+// the caller.
+static __device__ __align__(256) unsigned char g_qv_noalloc_scratch[QV_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+
+constexpr int kNoallocMaxDevices = 64;
+constexpr size_t kNoallocHeader = 256;  // work counter + 4 error words, padded
+std::mutex g_noalloc_mu;
+unsigned char* g_noalloc_base[kNoallocMaxDevices] = {};
+
+// Device address of g_qv_noalloc_scratch on `device` (which must be current).
+unsigned char* noalloc_base(int device) {
+  if (device < 0 || device >= kNoallocMaxDevices)
+    fail(QV_ERR_UNSUPPORTED, "qv_search_noalloc supports CUDA ordinals below 64");
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_base[device]) {
+    void* ptr = nullptr;
+    const cudaError_t rc = cudaGetSymbolAddress(&ptr, g_qv_noalloc_scratch);
+    if (rc != cudaSuccess)
+      fail(QV_ERR_CUDA, std::string("cudaGetSymbolAddress(g_qv_noalloc_scratch) failed: ") + cudaGetErrorString(rc));
+    g_noalloc_base[device] = static_cast<unsigned char*>(ptr);
+  }
+  return g_noalloc_base[device];
+}
+
+size_t align256(size_t v) { return (v + 255) / 256 * 256; }
+
+}  // namespace
+
+int qv_search_noalloc(qv_engine* e, const float* queries, int64_t nq, int64_t dim, const qv_search_opts* opts,
+                      int32_t* ids, float* dists, int32_t* found) {
+  return guarded([&] {
+    if (!e || !opts || (nq > 0 && (!queries || !ids || !dists))) fail(QV_ERR_INVALID_ARG, "null argument");
+    if (nq < 0) fail(QV_ERR_INVALID_ARG, "nq must be non-negative");
+    if (dim != e->L.dim)
+      fail(QV_ERR_INVALID_ARG, "Query dimension mismatch: queries have " + std::to_string(dim) +
+                                   " dims, but the index expects " + std::to_string(e->L.dim));
+    CK(cudaSetDevice(e->device));
+    const Plan pl = make_plan(e, *opts, std::max<int64_t>(nq, 1));
+    if (nq == 0) return;
+    const size_t k = static_cast<size_t>(opts->topk);
+    const size_t q_bytes = align256(static_cast<size_t>(nq) * dim * 4);
+    const size_t r_bytes = align256(static_cast<size_t>(nq) * k * 4);
+    const size_t f_bytes = align256(static_cast<size_t>(nq) * 4);
+    const size_t need = kNoallocHeader + q_bytes + 2 * r_bytes + f_bytes;
+    if (need > QV_NOALLOC_SCRATCH_BYTES)
+      fail(QV_ERR_INVALID_ARG, "qv_search_noalloc: " + std::to_string(nq) + " queries need " + std::to_string(need) +
+                                   " bytes of scratch, above its " + std::to_string(QV_NOALLOC_SCRATCH_BYTES) +
+                                   "-byte maximum; split the batch or use qv_search");
+    unsigned char* base = noalloc_base(e->device);
+    int32_t* counters = reinterpret_cast<int32_t*>(base);
+    float* d_q = reinterpret_cast<float*>(base + kNoallocHeader);
+    int32_t* d_ids = reinterpret_cast<int32_t*>(base + kNoallocHeader + q_bytes);
+    float* d_dists = reinterpret_cast<float*>(base + kNoallocHeader + q_bytes + r_bytes);
+    int32_t* d_found = reinterpret_cast<int32_t*>(base + kNoallocHeader + q_bytes + 2 * r_bytes);
+    cudaStream_t st = e->stream;
+    CK(cudaMemsetAsync(counters, 0, 8 * sizeof(int32_t), st));
+    CK(cudaMemcpyAsync(d_q, queries, static_cast<size_t>(nq) * dim * 4, cudaMemcpyHostToDevice, st));
+    qvk::SearchParams p = make_params(e, pl, *opts, d_q, nq, d_ids, d_dists, d_found, nullptr, nullptr);
+    p.work_counter = counters;
+    p.error_info = counters + 1;
+    pl.launch(p, pl.grid, pl.threads, pl.smem, st);
+    CK(cudaGetLastError());
+    CK(cudaMemcpyAsync(ids, d_ids, static_cast<size_t>(nq) * k * 4, cudaMemcpyDeviceToHost, st));
+    CK(cudaMemcpyAsync(dists, d_dists, static_cast<size_t>(nq) * k * 4, cudaMemcpyDeviceToHost, st));
+    if (found) CK(cudaMemcpyAsync(found, d_found, static_cast<size_t>(nq) * 4, cudaMemcpyDeviceToHost, st));
+    int32_t info[4];
+    CK(cudaMemcpyAsync(info, counters + 1, sizeof(info), cudaMemcpyDeviceToHost, st));
+    CK(cudaStreamSynchronize(st));
+    if (info[0] != qvk::kErrNone)
+      fail(QV_ERR_DEVICE, "search kernel reported device error " + std::to_string(info[0]) + " (query " +
+                              std::to_string(info[1]) + ")");
+  });
+}
 int qv_build_lut_device(qv_engine* e, const float* d_queries, int64_t nq, float* d_lut, float* d_q2,
                         void* stream) {
   return guarded([&] {

@@ -81,6 +81,8 @@ ENGINE_SYMBOLS = {
                                   C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.POINTER(SearchStats)]),
     "qv_search_device": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int64, C.POINTER(SearchOpts), C.c_void_p,
                                    C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
+    "qv_search_noalloc": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int64, C.c_int64, C.POINTER(SearchOpts),
+                                    C.c_void_p, C.c_void_p, C.c_void_p]),
     "qv_check_device_status": (C.c_int, [C.c_void_p]),
     "qv_plan": (C.c_int, [C.c_void_p, C.POINTER(SearchOpts), C.c_int64, C.POINTER(SearchStats)]),
     "qv_build_lut_device": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int64, C.c_void_p, C.c_void_p, C.c_void_p]),

@@ -150,6 +150,21 @@ class Engine:
                                          C.c_void_p(found.ctypes.data), C.c_void_p(ms.ctypes.data), C.byref(st)))
         return ids, dists, found, ms, st
 
+    def search_noalloc(self, queries: np.ndarray, params: SearchParams | None = None):
+        """qv_search_noalloc: the same search with no device allocation on the call
+        path (its scratch is a fixed 4 MiB device array); returns (ids, dists, found)."""
+        params = params or SearchParams()
+        q = np.ascontiguousarray(queries, dtype=np.float32)
+        nq, dim = q.shape
+        ids = np.empty((nq, params.topk), dtype=np.int32)
+        dists = np.empty((nq, params.topk), dtype=np.float32)
+        found = np.empty(nq, dtype=np.int32)
+        o = params.to_c()
+        _check(self._lib.qv_search_noalloc(self._h, C.c_void_p(q.ctypes.data), nq, dim, C.byref(o),
+                                           C.c_void_p(ids.ctypes.data), C.c_void_p(dists.ctypes.data),
+                                           C.c_void_p(found.ctypes.data)))
+        return ids, dists, found
+
     def search_host_ptrs(self, q_ptr: int, nq: int, dim: int, params: SearchParams, ids_ptr: int,
                          dists_ptr: int, found_ptr: int | None = None) -> None:
         """qv_search on raw host pointers (e.g. pinned torch tensors)."""
