@@ -149,13 +149,11 @@ Plan make_plan(qv_engine* e, const qv_search_opts& o, int64_t nq) {
   y.off_lid = take(int64_t(o.ef_search) * 4);
   y.off_ldist = take(int64_t(o.ef_search) * 4);
   if (pl.block) {
-    y.off_nid = take(int64_t(G) * rp * 4);    // new pairs, per-warp sorted runs
-    y.off_ndist = take(int64_t(G) * rp * 4);
-    y.off_spos = take(int64_t(G) * rp * 4);   // new pairs of each record in key order (ids)
-    y.off_sflag = take(int64_t(G) * rp * 4);  //   (distances)
+    y.off_spos = take(rp * 4);    // the current record's new pairs by neighbour slot (distances)
+    y.off_sflag = take(rp * 4);   //   (ids)
     y.off_S = take(rp * 4);
     y.off_fsrc = take(rp * 4);
-    y.off_misc = take(32 * 4);
+    y.off_misc = take(64 * 4);
   } else {
     y.off_nid = take(rp * 4);
     y.off_ndist = take(rp * 4);

@@ -31,7 +31,6 @@
 namespace qvk {
 
 constexpr int kBlock = 128;
-constexpr int kGpThread = 96;     // warp 3, lane 0: gpruning state and counters
 constexpr int kFastEntries = 4;   // list entries per thread held in registers (ef <= 512)
 
 // block scalars (misc[])
@@ -47,6 +46,17 @@ enum : int {
   kMiscNode = 16,   // [4] node of each record of the group
   kMiscWs = 20,     // [4] lane of each record of the group
   kMiscFu = 24,     // [4] per-warp first unvisited old entry at or after the hint
+  kMiscMask = 28,   // [4] per-warp survivor ballots
+  kMiscTwin = 32,   // 1 when a new pair repeats an earlier new pair's id
+  kMiscTwinMask = 36,  // [4] per-warp ballots of such repeats
+  kMiscStep = 40,
+  kMiscCnt = 41,
+  kMiscLastFc = 42,
+  kMiscLastTop1 = 43,  // float bits
+  kMiscLastTopk = 44,  // float bits
+  kMiscNbrsLo = 45,
+  kMiscNbrsHi = 46,
+  kMiscWords = 48,
 };
 
 struct BSlot {
@@ -54,12 +64,10 @@ struct BSlot {
   float* q2;
   uint32_t* lid;
   float* ldist;
-  float* nd;        // [G * RP] new pairs, per-warp sorted runs
-  uint32_t* ni;
-  float* sd;        // [G * RP] new pairs of each record in key order
+  float* sd;        // [RP] the current record's new pairs by neighbour slot
   uint32_t* si;
   int* S;           // [RP] insertion points of the survivors, ascending
-  int* fsrc;        // [RP] index in sd/si of the j-th survivor
+  int* fsrc;        // [RP] neighbour slot of the j-th survivor
   int32_t* rid;
   float* rdist;
   uint8_t* rec;
@@ -73,8 +81,6 @@ __device__ __forceinline__ BSlot make_bslot(uint8_t* base, const SlotLayout& L) 
   s.q2 = reinterpret_cast<float*>(base + L.off_q2);
   s.lid = reinterpret_cast<uint32_t*>(base + L.off_lid);
   s.ldist = reinterpret_cast<float*>(base + L.off_ldist);
-  s.nd = reinterpret_cast<float*>(base + L.off_ndist);
-  s.ni = reinterpret_cast<uint32_t*>(base + L.off_nid);
   s.sd = reinterpret_cast<float*>(base + L.off_spos);
   s.si = reinterpret_cast<uint32_t*>(base + L.off_sflag);
   s.S = reinterpret_cast<int*>(base + L.off_S);
@@ -141,13 +147,6 @@ __device__ __forceinline__ void build_lut_block(const SearchParams& p, const flo
   __syncthreads();
 }
 
-// Per-query state that only kGpThread keeps (gpruning, counters).
-struct BlockQuery {
-  int step, cnt, last_fc;
-  float last_top1, last_topk;
-  int64_t nbrs;
-};
-
 // Warp 0: first unvisited entry at or after the hint; marks it, advances the
 // hint and stores the result in lane[w] (-1 instead when the query stopped).
 __device__ __forceinline__ void select_block_warp(const BSlot& s, int w, int lane) {
@@ -177,11 +176,13 @@ __device__ __forceinline__ void select_block_warp(const BSlot& s, int w, int lan
   __syncwarp();
 }
 
-// Warp 3: exact distance of the expanded node into the top-k, then the step
-// count and gpruning (kernel_q1.cuh:524-545) on lane 0.
+// One warp: exact distance of the expanded node into the top-k, then the
+// step count and gpruning (kernel_q1.cuh:524-545) on its lane 0.  The
+// per-query counters live in misc[] because the visiting warp changes with
+// the record.
 template <typename T>
 __device__ __forceinline__ void visit_warp(const SearchParams& p, const BSlot& s, int gg, int node, int deg,
-                                           BlockQuery& bq, int lane) {
+                                           int lane) {
   const float dx = exact_l2_warp<T>(s.q2, reinterpret_cast<const T*>(s.rec + gg * p.lay.rec_stride), p.dim, lane);
   int fc = s.misc[kMiscFc];
   if (fc < p.k || dx < s.rdist[p.k - 1]) {
@@ -189,49 +190,65 @@ __device__ __forceinline__ void visit_warp(const SearchParams& p, const BSlot& s
     if (lane == 0) s.misc[kMiscFc] = fc;
   }
   if (lane == 0) {
-    bq.step += 1;
-    bq.nbrs += deg;
+    const int step = s.misc[kMiscStep] + 1;
+    s.misc[kMiscStep] = step;
+    const uint64_t nb = (static_cast<uint64_t>(static_cast<uint32_t>(s.misc[kMiscNbrsHi])) << 32 |
+                         static_cast<uint32_t>(s.misc[kMiscNbrsLo])) + static_cast<uint64_t>(deg);
+    s.misc[kMiscNbrsLo] = static_cast<int>(static_cast<uint32_t>(nb));
+    s.misc[kMiscNbrsHi] = static_cast<int>(static_cast<uint32_t>(nb >> 32));
     if (p.early_policy != 0) {
       const float top1 = s.rdist[0];
       const float topk = s.rdist[p.k - 1];
-      const bool improved = fc > bq.last_fc || top1 < bq.last_top1 || topk < bq.last_topk;
-      if (bq.step < p.gp_warmup)
-        bq.cnt = 0;
+      const bool improved = fc > s.misc[kMiscLastFc] || top1 < __int_as_float(s.misc[kMiscLastTop1]) ||
+                            topk < __int_as_float(s.misc[kMiscLastTopk]);
+      int cnt = s.misc[kMiscCnt];
+      if (step < p.gp_warmup)
+        cnt = 0;
       else
-        bq.cnt = improved ? 0 : bq.cnt + 1;
-      bq.last_fc = fc;
-      bq.last_top1 = top1;
-      bq.last_topk = topk;
-      if (p.early_policy == 2 && bq.step >= p.gp_warmup && p.gp_patience > 0 && bq.cnt >= p.gp_patience)
+        cnt = improved ? 0 : cnt + 1;
+      s.misc[kMiscCnt] = cnt;
+      s.misc[kMiscLastFc] = fc;
+      s.misc[kMiscLastTop1] = __float_as_int(top1);
+      s.misc[kMiscLastTopk] = __float_as_int(topk);
+      if (p.early_policy == 2 && step >= p.gp_warmup && p.gp_patience > 0 && cnt >= p.gp_patience)
         s.misc[kMiscStop] = 1;
     }
   }
 }
 
 // Merge record gg of the current group into the list, visit its node, and
-// select the lane's next node.
+// select the lane's next node.  (d, id) is this thread's new pair when it
+// owns one of record gg's neighbours (owner), else ignored.
 template <typename T, int RP>
-__device__ __forceinline__ void merge_visit_select(const SearchParams& p, const BSlot& s, int gg,
-                                                   BlockQuery& bq) {
+__device__ __forceinline__ void merge_visit_select(const SearchParams& p, const BSlot& s, int gg, bool owner,
+                                                   bool live, float d, uint32_t id) {
+  constexpr int NW = RP / 32;  // warps that hold one record's pairs
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int e = tid % RP;
   const int sz = s.misc[kMiscSize];
   const int h = s.misc[kMiscHint];
   const int deg = s.misc[kMiscDeg + gg];
   const int node = s.misc[kMiscNode + gg];
   const int w = s.misc[kMiscWs + gg];
-  const float* sd = s.sd + gg * RP;
-  const uint32_t* si = s.si + gg * RP;
+  const int vwarp = (kBlock / RP == 2 && gg == 1) ? 0 : 3;  // a warp that owns none of this record's pairs
+  float* kd = s.sd;    // [RP] this record's pairs by neighbour slot
+  uint32_t* ki = s.si;
   const bool fast = sz <= kBlock * kFastEntries;
 
-  // Phase A: insertion points, survivors, reads of the old entries, visit.
+  // Phase A: pairs worse than the last entry of a full list cannot enter it;
+  // the others find their insertion point and drop out when their id is
+  // already listed.  Old entries are read, the node is visited.
   bool surv = false;
   int r = 0;
-  if (tid < deg) {
-    const float kd = sd[tid];
-    const uint32_t ki = si[tid];
-    const bool twin = tid > 0 && si[tid - 1] == ki;
-    r = lower_bound_s(s.ldist, s.lid, sz, kd, ki);
-    surv = !twin && !(r < sz && ((s.lid[r] ^ ki) & kIdMask) == 0);
+  if (owner && live) {
+    bool cand = true;
+    if (sz == p.ef) cand = key_less(d, id, s.ldist[sz - 1], s.lid[sz - 1]);
+    if (cand) {
+      r = lower_bound_s(s.ldist, s.lid, sz, d, id);
+      surv = !(r < sz && ((s.lid[r] ^ id) & kIdMask) == 0);
+    }
+    kd[e] = d;
+    ki[e] = id;
   }
   const unsigned bal = __ballot_sync(kFull, surv);
   uint32_t vid[kFastEntries];
@@ -239,41 +256,98 @@ __device__ __forceinline__ void merge_visit_select(const SearchParams& p, const 
   int fu = 0x7fffffff;
   if (fast) {
 #pragma unroll
-    for (int e = 0; e < kFastEntries; ++e) {
-      const int i = tid + kBlock * e;
-      vid[e] = 0;
-      vd[e] = 0.f;
+    for (int x = 0; x < kFastEntries; ++x) {
+      const int i = tid + kBlock * x;
+      vid[x] = 0;
+      vd[x] = 0.f;
       if (i < sz) {
-        vid[e] = s.lid[i];
-        vd[e] = s.ldist[i];
-        if (i >= h && (vid[e] & kVisited) == 0) fu = min(fu, i);
+        vid[x] = s.lid[i];
+        vd[x] = s.ldist[i];
+        if (i >= h && (vid[x] & kVisited) == 0) fu = min(fu, i);
       }
     }
     fu = __reduce_min_sync(kFull, fu);
   }
   if (lane == 0) {
-    s.misc[kMiscWtot + warp] = __popc(bal);
+    s.misc[kMiscMask + warp] = static_cast<int>(bal);
     s.misc[kMiscFu + warp] = fu;
   }
-  if (warp == 3) visit_warp<T>(p, s, gg, node, deg, bq, lane);
+  if (warp == vwarp) visit_warp<T>(p, s, gg, node, deg, lane);
   __syncthreads();
 
-  // Phase B: survivor ranks by a block prefix count.
-  int before = 0, nsurv = 0;
+  // Phase B: survivors rank themselves among the survivors (ties, which only
+  // a repeated id produces, by neighbour slot).  A pair repeating an earlier
+  // survivor's id marks itself; when any does, the ranks are redone without
+  // them, so only the first copy enters (the reference's compaction keeps
+  // one of adjacent equal ids).
+  unsigned masks[NW];
+  int nsurv = 0;
+#pragma unroll
+  for (int x = 0; x < NW; ++x) {
+    masks[x] = static_cast<unsigned>(s.misc[kMiscMask + gg * NW + x]);
+    nsurv += __popc(masks[x]);
+  }
   fu = 0x7fffffff;
 #pragma unroll
-  for (int x = 0; x < 4; ++x) {
-    const int t = s.misc[kMiscWtot + x];
-    before += (x < warp) ? t : 0;
-    nsurv += t;
-    fu = min(fu, s.misc[kMiscFu + x]);
-  }
+  for (int x = 0; x < 4; ++x) fu = min(fu, s.misc[kMiscFu + x]);
   if (surv) {
-    const int j = before + __popc(bal & ((1u << lane) - 1u));
-    s.S[j] = r;
-    s.fsrc[j] = tid;
+    int rank = 0;
+    bool twin = false;
+#pragma unroll
+    for (int x = 0; x < NW; ++x) {
+      unsigned m = masks[x];
+      while (m) {
+        const int u = x * 32 + __ffs(m) - 1;
+        m &= m - 1;
+        if (u == e) continue;
+        const float du = kd[u];
+        const uint32_t iu = ki[u];
+        if (key_less(du, iu, d, id)) {
+          ++rank;
+        } else if (!key_less(d, id, du, iu) && u < e) {
+          ++rank;
+          twin = true;
+        }
+      }
+    }
+    s.S[rank] = r;
+    s.fsrc[rank] = e;
+    if (twin) {
+      s.misc[kMiscTwin] = 1;
+      atomicOr(reinterpret_cast<unsigned*>(&s.misc[kMiscTwinMask + (e >> 5)]), 1u << (e & 31));
+    }
   }
   __syncthreads();
+  if (s.misc[kMiscTwin]) {  // rare: an adjacency list repeats an id
+#pragma unroll
+    for (int x = 0; x < NW; ++x) masks[x] &= ~static_cast<unsigned>(s.misc[kMiscTwinMask + x]);
+    const bool keep = surv && !((static_cast<unsigned>(s.misc[kMiscTwinMask + (e >> 5)]) >> (e & 31)) & 1u);
+    nsurv = 0;
+#pragma unroll
+    for (int x = 0; x < NW; ++x) nsurv += __popc(masks[x]);
+    __syncthreads();
+    if (keep) {
+      int rank = 0;
+#pragma unroll
+      for (int x = 0; x < NW; ++x) {
+        unsigned m = masks[x];
+        while (m) {
+          const int u = x * 32 + __ffs(m) - 1;
+          m &= m - 1;
+          if (u != e && key_less(kd[u], ki[u], d, id)) ++rank;
+        }
+      }
+      s.S[rank] = r;
+      s.fsrc[rank] = e;
+    }
+    surv = keep;
+    __syncthreads();
+    if (tid == 0) {
+      s.misc[kMiscTwin] = 0;
+#pragma unroll
+      for (int x = 0; x < NW; ++x) s.misc[kMiscTwinMask + x] = 0;
+    }
+  }
 
   const int nsize = min(sz + nsurv, p.ef);
   const bool stopped = s.misc[kMiscStop] != 0;
@@ -285,16 +359,16 @@ __device__ __forceinline__ void merge_visit_select(const SearchParams& p, const 
     if (fu != 0x7fffffff) sel = min(sel, fu + count_le(s.S, nsurv, fu));
     if (sel >= nsize) sel = -1;
 #pragma unroll
-    for (int e = 0; e < kFastEntries; ++e) {
-      const int i = tid + kBlock * e;
+    for (int x = 0; x < kFastEntries; ++x) {
+      const int i = tid + kBlock * x;
       if (i < sz) {
         const int dst = i >= first ? i + count_le(s.S, nsurv, i) : i;
         const bool mark = dst == sel;
         if (dst < p.ef && (dst != i || mark)) {
-          s.lid[dst] = vid[e] | (mark ? kVisited : 0u);
-          s.ldist[dst] = vd[e];
+          s.lid[dst] = vid[x] | (mark ? kVisited : 0u);
+          s.ldist[dst] = vd[x];
         }
-        if (mark && !stopped) s.lane[w] = static_cast<int32_t>(vid[e] & kIdMask);
+        if (mark && !stopped) s.lane[w] = static_cast<int32_t>(vid[x] & kIdMask);
       }
     }
     if (tid < nsurv) {
@@ -302,9 +376,9 @@ __device__ __forceinline__ void merge_visit_select(const SearchParams& p, const 
       if (fp < p.ef) {
         const int src = s.fsrc[tid];
         const bool mark = fp == sel;
-        s.lid[fp] = si[src] | (mark ? kVisited : 0u);
-        s.ldist[fp] = sd[src];
-        if (mark && !stopped) s.lane[w] = static_cast<int32_t>(si[src]);
+        s.lid[fp] = ki[src] | (mark ? kVisited : 0u);
+        s.ldist[fp] = kd[src];
+        if (mark && !stopped) s.lane[w] = static_cast<int32_t>(ki[src]);
       }
     }
     if (tid == 0) {
@@ -343,8 +417,8 @@ __device__ __forceinline__ void merge_visit_select(const SearchParams& p, const 
       const int fp = s.S[tid] + tid;
       if (fp < p.ef) {
         const int src = s.fsrc[tid];
-        s.lid[fp] = si[src];
-        s.ldist[fp] = sd[src];
+        s.lid[fp] = ki[src];
+        s.ldist[fp] = kd[src];
       }
     }
     if (tid == 0) {
@@ -359,7 +433,7 @@ __device__ __forceinline__ void merge_visit_select(const SearchParams& p, const 
 
 // Expand the lanes in `mask`, in lane order, G = 128 / RP records at a time.
 template <typename T, int MC, int RP>
-__device__ int expand_block(const SearchParams& p, const BSlot& s, uint32_t mask, int64_t qid, BlockQuery& bq) {
+__device__ int expand_block(const SearchParams& p, const BSlot& s, uint32_t mask, int64_t qid) {
   constexpr int G = kBlock / RP;
   constexpr int NV = MC > 0 ? MC / 16 : 1;
   const int tid = threadIdx.x;
@@ -419,37 +493,9 @@ __device__ int expand_block(const SearchParams& p, const BSlot& s, uint32_t mask
         d = acc;
       }
     }
-    {  // each warp sorts its 32 pairs; padding (inf, 0xffffffff) sorts last
-      float kd[1] = {d};
-      uint32_t ki[1] = {live ? nb : 0xffffffffu};
-      bitonic_sort<1>(kd, ki, tid & 31);
-      s.nd[tid] = kd[0];
-      s.ni[tid] = ki[0];
-    }
     __syncthreads();
     if (s.misc[kMiscErr]) return s.misc[kMiscErr];
-    {  // merge the runs of each record into key order: rank = index in run +
-       // pairs below it in the other runs (lower runs win ties)
-      const float kd = s.nd[tid];
-      const uint32_t ki = s.ni[tid];
-      if (ki != 0xffffffffu) {
-        const int run = e >> 5, i = e & 31;
-        int rank = i;
-#pragma unroll
-        for (int o = 0; o < RP / 32; ++o) {
-          if (o == run) continue;
-          const float* od = s.nd + g * RP + (o << 5);
-          const uint32_t* oi = s.ni + g * RP + (o << 5);
-          const int lb = lower_bound_s(od, oi, 32, kd, ki);
-          const bool eq = o < run && lb < 32 && od[lb] == kd && ((oi[lb] ^ ki) & kIdMask) == 0;
-          rank += lb + (eq ? 1 : 0);
-        }
-        s.sd[g * RP + rank] = kd;
-        s.si[g * RP + rank] = ki;
-      }
-    }
-    __syncthreads();
-    for (int gg = 0; gg < gact; ++gg) merge_visit_select<T, RP>(p, s, gg, bq);
+    for (int gg = 0; gg < gact; ++gg) merge_visit_select<T, RP>(p, s, gg, g == gg, live, d, nb);
   }
   return 0;
 }
@@ -464,23 +510,11 @@ __device__ void run_query_block(const SearchParams& p, const BSlot& s, int64_t q
     s.rdist[i] = __int_as_float(0x7f800000);
   }
   if (tid < kMaxPipeWidth) s.lane[tid] = (tid == 0) ? p.medoid : -1;
-  if (tid == 0) {
-    s.misc[kMiscErr] = 0;
-    s.misc[kMiscSize] = 0;
-    s.misc[kMiscHint] = 0;
-    s.misc[kMiscFc] = 0;
-    s.misc[kMiscStop] = 0;
-  }
-  BlockQuery bq;
-  bq.step = 0;
-  bq.cnt = 0;
-  bq.last_fc = 0;
-  bq.last_top1 = __int_as_float(0x7f800000);
-  bq.last_topk = __int_as_float(0x7f800000);
-  bq.nbrs = 0;
+  if (tid < kMiscWords && tid != kMiscQid) s.misc[tid] = 0;
+  if (tid == kMiscLastTop1 || tid == kMiscLastTopk) s.misc[tid] = 0x7f800000;  // +inf
   __syncthreads();
 
-  int err = expand_block<T, MC, RP>(p, s, 1u, qid, bq);  // boot: the entry on lane 0
+  int err = expand_block<T, MC, RP>(p, s, 1u, qid);  // boot: the entry on lane 0
   if (!err) {
     // lanes 1..W-1 are seeded whether or not the boot hop stopped the query
     // (kernel_q1.cuh:367-371); their picks matter only when it did not
@@ -499,7 +533,7 @@ __device__ void run_query_block(const SearchParams& p, const BSlot& s, int64_t q
         break;
       }
       __syncthreads();  // everyone has read lane[] before it changes
-      err = expand_block<T, MC, RP>(p, s, active, qid, bq);
+      err = expand_block<T, MC, RP>(p, s, active, qid);
       if (err || s.misc[kMiscStop]) break;
       if (warp == 0)
         for (int w = 0; w < p.W; ++w)
@@ -511,17 +545,19 @@ __device__ void run_query_block(const SearchParams& p, const BSlot& s, int64_t q
     p.out_ids[qid * p.k + i] = s.rid[i];
     p.out_dists[qid * p.k + i] = s.rdist[i];
   }
-  if (tid == kGpThread) {
+  if (tid == 0) {
     if (p.out_found) p.out_found[qid] = err ? -1 : s.misc[kMiscFc];
-    if (p.out_steps) p.out_steps[qid] = bq.step;
-    if (p.out_nbrs) p.out_nbrs[qid] = bq.nbrs;
+    if (p.out_steps) p.out_steps[qid] = s.misc[kMiscStep];
+    if (p.out_nbrs)
+      p.out_nbrs[qid] = static_cast<int64_t>(static_cast<uint64_t>(static_cast<uint32_t>(s.misc[kMiscNbrsHi])) << 32 |
+                                             static_cast<uint32_t>(s.misc[kMiscNbrsLo]));
     if (p.out_time) p.out_time[2 * qid + 1] = globaltimer_ns();
   }
   __syncthreads();
 }
 
 template <typename T, int MC, int RP>
-__global__ void __launch_bounds__(kBlock) search_block_kernel(const SearchParams p) {
+__global__ void __launch_bounds__(kBlock, 5) search_block_kernel(const SearchParams p) {
   extern __shared__ __align__(16) uint8_t smem[];
   const BSlot s = make_bslot(smem, p.lay);
   while (true) {

@@ -53,11 +53,11 @@ struct SlotLayout {
   int32_t rec_stride;            // bytes per staged vector, multiple of 16
   int32_t off_lane;              // int [W] pending node per pipe lane
   // block kernel only
-  int32_t off_spos;              // float [G*RP] new pairs of each record in key order (distances)
-  int32_t off_sflag;             // uint [G*RP]   (ids)
+  int32_t off_spos;              // float [RP] the current record's new pairs by neighbour slot
+  int32_t off_sflag;             // uint [RP]   (their ids)
   int32_t off_S;                 // int [RP] insertion points of the surviving pairs, ascending
-  int32_t off_fsrc;              // int [RP] key-order index of the j-th survivor
-  int32_t off_misc;              // int [32] block scalars
+  int32_t off_fsrc;              // int [RP] neighbour slot of the j-th survivor
+  int32_t off_misc;              // int [64] block scalars
 };
 
 struct SearchParams {

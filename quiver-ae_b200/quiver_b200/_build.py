@@ -66,11 +66,13 @@ def _headers() -> list[Path]:
 
 def build_engine(force: bool = False, verbose: bool = False) -> Path:
     """Compile libquiver_b200.so (sm_100a)."""
+    units = ["engine.cu", "search_u8.cu", "search_i8.cu", "search_f32.cu", "index_io.cpp"]
+    headers = _headers()
+    if not force and ENGINE_LIB.exists() and not _newer(ENGINE_LIB, [CSRC / u for u in units] + headers):
+        return ENGINE_LIB
     LIB_DIR.mkdir(exist_ok=True)
     OBJ_DIR.mkdir(exist_ok=True)
     nvcc = _nvcc()
-    units = ["engine.cu", "search_u8.cu", "search_i8.cu", "search_f32.cu", "index_io.cpp"]
-    headers = _headers()
     jobs = []
     objs = []
     for u in units:
