@@ -149,11 +149,12 @@ Plan make_plan(qv_engine* e, const qv_search_opts& o, int64_t nq) {
   y.off_lid = take(int64_t(o.ef_search) * 4);
   y.off_ldist = take(int64_t(o.ef_search) * 4);
   if (pl.block) {
-    y.off_spos = take(rp * 4);    // the current record's new pairs by neighbour slot (distances)
-    y.off_sflag = take(rp * 4);   //   (ids)
-    y.off_S = take(rp * 4);
-    y.off_fsrc = take(rp * 4);
-    y.off_misc = take(64 * 4);
+    y.off_spos = take(qvk::kBlock * 4);   // new pairs by thread slot (distances)
+    y.off_sflag = take(qvk::kBlock * 4);  //   (ids)
+    y.off_r0 = take(qvk::kBlock * 4);     //   (insertion points)
+    y.off_S = take(qvk::kBlock * 4);
+    y.off_fsrc = take(qvk::kBlock * 4);
+    y.off_misc = take(qvk::kMiscSlots * 4);
   } else {
     y.off_nid = take(rp * 4);
     y.off_ndist = take(rp * 4);

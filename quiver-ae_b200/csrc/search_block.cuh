@@ -56,7 +56,19 @@ enum : int {
   kMiscLastTopk = 44,  // float bits
   kMiscNbrsLo = 45,
   kMiscNbrsHi = 46,
-  kMiscWords = 48,
+  kMiscWords = 48,  // words zeroed at the start of a query
+  // group merge (merge_group)
+  kMiscGMask = 48,  // [4] per-warp ballots of the pairs that may enter the list
+  kMiscGFu1 = 52,   // [4] per-warp first unvisited entry at or after the hint
+  kMiscGFu2 = 56,   // [4] per-warp second one
+  kMiscGNs = 60,    // surviving pairs after removing repeated ids
+  kMiscGPos0 = 61,  // final position of the first record's pick (-1: none or cut)
+  kMiscGPos1 = 62,  // final position of the second record's pick (-1: none or cut)
+  kMiscGStop0 = 63, // stop flag right after the first record's visit
+  kMiscGId0 = 64,   // first record's pick (-1: none)
+  kMiscGId1 = 65,   // second record's pick (-1: none)
+  kMiscGHint = 66,  // hint after the merge
+  kMiscSlots = 80,
 };
 
 struct BSlot {
@@ -64,10 +76,11 @@ struct BSlot {
   float* q2;
   uint32_t* lid;
   float* ldist;
-  float* sd;        // [RP] the current record's new pairs by neighbour slot
+  float* sd;        // [128] new pairs by thread slot
   uint32_t* si;
-  int* S;           // [RP] insertion points of the survivors, ascending
-  int* fsrc;        // [RP] neighbour slot of the j-th survivor
+  int* r0;          // [128] their insertion points in the list
+  int* S;           // [128] insertion points of the survivors, ascending
+  int* fsrc;        // [128] thread slot of the j-th survivor
   int32_t* rid;
   float* rdist;
   uint8_t* rec;
@@ -83,6 +96,7 @@ __device__ __forceinline__ BSlot make_bslot(uint8_t* base, const SlotLayout& L) 
   s.ldist = reinterpret_cast<float*>(base + L.off_ldist);
   s.sd = reinterpret_cast<float*>(base + L.off_spos);
   s.si = reinterpret_cast<uint32_t*>(base + L.off_sflag);
+  s.r0 = reinterpret_cast<int*>(base + L.off_r0);
   s.S = reinterpret_cast<int*>(base + L.off_S);
   s.fsrc = reinterpret_cast<int*>(base + L.off_fsrc);
   s.rid = reinterpret_cast<int32_t*>(base + L.off_rid);
@@ -431,6 +445,256 @@ __device__ __forceinline__ void merge_visit_select(const SearchParams& p, const 
   __syncthreads();
 }
 
+// Position (0-based) of the n-th set bit of m; n < popc(m).
+__device__ __forceinline__ int nth_set_bit(unsigned m, int n) {
+  int pos = 0;
+#pragma unroll
+  for (int w = 16; w >= 1; w >>= 1) {
+    const int c = __popc(m & ((1u << w) - 1u));
+    if (n >= c) {
+      n -= c;
+      m >>= w;
+      pos += w;
+    }
+  }
+  return pos;
+}
+
+// Merge the records of one group (one or two pipe lanes, in lane order) into
+// the list in a single pass, visit their nodes and pick each lane's next node.
+//
+// Applying the records one after the other keeps the first ef entries of
+// "list + first record's pairs" and then the first ef of "that + second
+// record's pairs", dropping pairs whose id is already present.  An id always
+// has the same key within a query, so this equals the first ef entries of the
+// union of the list and both records' pairs with repeated keys removed; a
+// pair that repeats a list entry or an earlier pair drops out, and an entry
+// that the first merge would cut is cut by the union's ef as well.  What
+// the order still decides is the visited marks: the first lane's pick is the
+// first unvisited entry of the list after the first record alone, and it is
+// marked before the second lane picks the first unvisited entry of the
+// union.  Both picks are computed from the insertion points below, before
+// anything moves.
+//
+// Returns false, having changed nothing, when more than 32 pairs survive the
+// filter (the opening hops of a query); the caller then merges the records
+// one by one.
+template <typename T, int RP>
+__device__ __forceinline__ bool merge_group(const SearchParams& p, const BSlot& s, int gact, bool live, float d,
+                                            uint32_t id) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int sz = s.misc[kMiscSize];
+  const int h = s.misc[kMiscHint];
+  const int ef = p.ef;
+
+  // Phase A: filter against a full list's last entry, insertion point, drop
+  // pairs whose id is listed; old entries into registers; the first two
+  // unvisited entries at or after the hint.
+  bool pre = false;
+  if (live) {
+    bool cand = true;
+    if (sz == ef) cand = key_less(d, id, s.ldist[sz - 1], s.lid[sz - 1]);
+    if (cand) {
+      const int r = lower_bound_s(s.ldist, s.lid, sz, d, id);
+      pre = !(r < sz && ((s.lid[r] ^ id) & kIdMask) == 0);
+      if (pre) {
+        s.sd[tid] = d;
+        s.si[tid] = id;
+        s.r0[tid] = r;
+      }
+    }
+  }
+  const unsigned bal = __ballot_sync(kFull, pre);
+  uint32_t vid[kFastEntries];
+  float vd[kFastEntries];
+  int f1 = 0x7fffffff, f2 = 0x7fffffff;
+#pragma unroll
+  for (int x = 0; x < kFastEntries; ++x) {
+    const int i = tid + kBlock * x;
+    vid[x] = 0;
+    vd[x] = 0.f;
+    if (i < sz) {
+      vid[x] = s.lid[i];
+      vd[x] = s.ldist[i];
+      if (i >= h && (vid[x] & kVisited) == 0) {
+        if (f1 == 0x7fffffff) f1 = i; else if (f2 == 0x7fffffff) f2 = i;
+      }
+    }
+  }
+  {
+    const int w1 = __reduce_min_sync(kFull, f1);
+    const int w2 = __reduce_min_sync(kFull, f1 == w1 ? f2 : f1);
+    if (lane == 0) {
+      s.misc[kMiscGMask + warp] = static_cast<int>(bal);
+      s.misc[kMiscGFu1 + warp] = w1;
+      s.misc[kMiscGFu2 + warp] = w2;
+    }
+  }
+  __syncthreads();
+
+  unsigned m[4];
+  int npre = 0;
+#pragma unroll
+  for (int x = 0; x < 4; ++x) {
+    m[x] = static_cast<unsigned>(s.misc[kMiscGMask + x]);
+    npre += __popc(m[x]);
+  }
+  if (npre > 32) return false;  // uniform: every thread read the same ballots
+
+  // Phase B: warp 0 ranks the surviving pairs and computes both picks; warp
+  // 1 visits the records' nodes in lane order.
+  if (warp == 0) {
+    int slot = -1;
+    float dd = 0.f;
+    uint32_t ii = 0;
+    int rr = 0;
+    if (lane < npre) {
+      int n = lane, base = 0;
+      unsigned mm = m[0];
+      if (n >= __popc(m[0])) {
+        n -= __popc(m[0]); mm = m[1]; base = 32;
+        if (n >= __popc(m[1])) {
+          n -= __popc(m[1]); mm = m[2]; base = 64;
+          if (n >= __popc(m[2])) { n -= __popc(m[2]); mm = m[3]; base = 96; }
+        }
+      }
+      slot = base + nth_set_bit(mm, n);
+      dd = s.sd[slot];
+      ii = s.si[slot];
+      rr = s.r0[slot];
+    }
+    unsigned lessm = 0, eqm = 0;
+    for (int j = 0; j < npre; ++j) {
+      const float dj = __shfl_sync(kFull, dd, j);
+      const uint32_t ij = __shfl_sync(kFull, ii, j);
+      if (key_less(dj, ij, dd, ii)) lessm |= 1u << j;
+      else if (j < lane && ((ij ^ ii) & kIdMask) == 0) eqm |= 1u << j;
+    }
+    const bool valid = lane < npre && eqm == 0;  // first copy of its id
+    const unsigned vm = __ballot_sync(kFull, valid);
+    const bool inA = slot < RP;                   // from the group's first record
+    const unsigned am = __ballot_sync(kFull, valid && inA);
+    const int rank = __popc(lessm & vm);
+    const int rankA = __popc(lessm & am);
+    if (valid) {
+      s.S[rank] = rr;
+      s.fsrc[rank] = slot;
+    }
+    // first two unvisited old entries at or after the hint
+    const int a = lane < 4 ? s.misc[kMiscGFu1 + lane] : 0x7fffffff;
+    const int b = lane < 4 ? s.misc[kMiscGFu2 + lane] : 0x7fffffff;
+    const int fu1 = __reduce_min_sync(kFull, a);
+    const int fu2 = __reduce_min_sync(kFull, a == fu1 ? b : a);
+    constexpr int kNone = 0x7fffffff;
+    // surviving pairs that land before old entry i
+    auto count_all = [&](int i) { return __popc(__ballot_sync(kFull, valid && rr <= i)); };
+    const unsigned bA = __ballot_sync(kFull, valid && inA && rankA == 0);
+    const unsigned b0 = __ballot_sync(kFull, valid && rank == 0);
+    const unsigned b1 = __ballot_sync(kFull, valid && rank == 1);
+    const int lA = bA ? __ffs(bA) - 1 : -1;
+    const int l0 = b0 ? __ffs(b0) - 1 : -1;
+    const int l1 = b1 ? __ffs(b1) - 1 : -1;
+    const int rA = __shfl_sync(kFull, rr, lA < 0 ? 0 : lA);
+    const uint32_t iA = __shfl_sync(kFull, ii, lA < 0 ? 0 : lA);
+    const int rank_lA = __shfl_sync(kFull, rank, lA < 0 ? 0 : lA);
+    const int cf1 = fu1 != kNone ? count_all(fu1) : 0;
+    const int cf2 = fu2 != kNone ? count_all(fu2) : 0;
+    // The first lane's pick: the first unvisited entry of "list + first
+    // record", i.e. the first record's smallest survivor or the first
+    // unvisited old entry, whichever has the smaller key (a survivor with
+    // insertion point r precedes old entry i exactly when r <= i).  Its
+    // position there is below ef: nothing of the first record precedes it.
+    int sel0 = -1;  // 0: survivor lA, 1: old entry fu1
+    int id0 = -1, pos0 = -1;
+    if (lA >= 0 && (fu1 == kNone || rA <= fu1)) {
+      sel0 = 0;
+      id0 = static_cast<int>(iA & kIdMask);
+      pos0 = rA + rank_lA;          // final position, counting the second record too
+    } else if (fu1 != kNone) {
+      sel0 = 1;
+      id0 = static_cast<int>(s.lid[fu1] & kIdMask);
+      pos0 = fu1 + cf1;
+    }
+    int id1 = -1, pos1 = -1;
+    if (gact == 2) {
+      // The second lane's pick: the first unvisited entry of the merged list
+      // once the first pick is marked.
+      const int ls = (sel0 == 0 && l0 == lA) ? l1 : l0;
+      const int lo = sel0 == 1 ? fu2 : fu1;
+      const int rs = __shfl_sync(kFull, rr, ls < 0 ? 0 : ls);
+      const int ks = __shfl_sync(kFull, rank, ls < 0 ? 0 : ls);
+      const uint32_t is = __shfl_sync(kFull, ii, ls < 0 ? 0 : ls);
+      if (ls >= 0 && (lo == kNone || rs <= lo)) {
+        pos1 = rs + ks;
+        id1 = static_cast<int>(is & kIdMask);
+      } else if (lo != kNone) {
+        pos1 = lo + (lo == fu1 ? cf1 : cf2);
+        id1 = static_cast<int>(s.lid[lo] & kIdMask);
+      }
+      if (pos1 >= ef) { pos1 = -1; id1 = -1; }
+    }
+    if (pos0 >= ef) pos0 = -1;  // picked, then cut by the second record
+    if (lane == 0) {
+      const int ns = __popc(vm);
+      const int nsize = min(sz + ns, ef);
+      s.misc[kMiscGNs] = ns;
+      s.misc[kMiscGPos0] = pos0;
+      s.misc[kMiscGPos1] = pos1;
+      s.misc[kMiscGId0] = id0;
+      s.misc[kMiscGId1] = id1;
+      s.misc[kMiscGHint] = gact == 2 ? (id1 >= 0 ? pos1 + 1 : nsize) : (id0 >= 0 ? pos0 + 1 : nsize);
+    }
+  } else if (warp == 1) {
+    visit_warp<T>(p, s, 0, s.misc[kMiscNode], s.misc[kMiscDeg], lane);
+    __syncwarp();
+    if (lane == 0) s.misc[kMiscGStop0] = s.misc[kMiscStop];
+    if (gact == 2) {
+      __syncwarp();
+      visit_warp<T>(p, s, 1, s.misc[kMiscNode + 1], s.misc[kMiscDeg + 1], lane);
+    }
+  }
+  __syncthreads();
+
+  // Phase C: shifted writes; the writers of the picks mark them.
+  const int ns = s.misc[kMiscGNs];
+  const int pos0 = s.misc[kMiscGPos0];
+  const int pos1 = s.misc[kMiscGPos1];
+  const int first = ns > 0 ? s.S[0] : 0x7fffffff;
+#pragma unroll
+  for (int x = 0; x < kFastEntries; ++x) {
+    const int i = tid + kBlock * x;
+    if (i < sz) {
+      const int dst = i >= first ? i + count_le(s.S, ns, i) : i;
+      const bool mark = dst == pos0 || dst == pos1;
+      if (dst < ef && (dst != i || mark)) {
+        s.lid[dst] = vid[x] | (mark ? kVisited : 0u);
+        s.ldist[dst] = vd[x];
+      }
+    }
+  }
+  if (tid < ns) {
+    const int fp = s.S[tid] + tid;
+    if (fp >= 0 && fp < ef) {
+      const int src = s.fsrc[tid];
+      const bool mark = fp == pos0 || fp == pos1;
+      s.lid[fp] = s.si[src] | (mark ? kVisited : 0u);
+      s.ldist[fp] = s.sd[src];
+    }
+  }
+  if (tid == 0) {
+    s.misc[kMiscSize] = min(sz + ns, ef);
+    s.misc[kMiscHint] = s.misc[kMiscGHint];
+    const int id0 = s.misc[kMiscGId0];
+    s.lane[s.misc[kMiscWs]] = (id0 >= 0 && !s.misc[kMiscGStop0]) ? id0 : -1;
+    if (gact == 2) {
+      const int id1 = s.misc[kMiscGId1];
+      s.lane[s.misc[kMiscWs + 1]] = (id1 >= 0 && !s.misc[kMiscStop]) ? id1 : -1;
+    }
+  }
+  __syncthreads();
+  return true;
+}
+
 // Expand the lanes in `mask`, in lane order, G = 128 / RP records at a time.
 template <typename T, int MC, int RP>
 __device__ int expand_block(const SearchParams& p, const BSlot& s, uint32_t mask, int64_t qid) {
@@ -495,6 +759,7 @@ __device__ int expand_block(const SearchParams& p, const BSlot& s, uint32_t mask
     }
     __syncthreads();
     if (s.misc[kMiscErr]) return s.misc[kMiscErr];
+    if (p.ef <= kBlock * kFastEntries && merge_group<T, RP>(p, s, gact, live, d, nb)) continue;
     for (int gg = 0; gg < gact; ++gg) merge_visit_select<T, RP>(p, s, gg, g == gg, live, d, nb);
   }
   return 0;

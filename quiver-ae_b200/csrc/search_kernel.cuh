@@ -53,11 +53,12 @@ struct SlotLayout {
   int32_t rec_stride;            // bytes per staged vector, multiple of 16
   int32_t off_lane;              // int [W] pending node per pipe lane
   // block kernel only
-  int32_t off_spos;              // float [RP] the current record's new pairs by neighbour slot
-  int32_t off_sflag;             // uint [RP]   (their ids)
-  int32_t off_S;                 // int [RP] insertion points of the surviving pairs, ascending
-  int32_t off_fsrc;              // int [RP] neighbour slot of the j-th survivor
-  int32_t off_misc;              // int [64] block scalars
+  int32_t off_spos;              // float [128] new pairs by thread slot
+  int32_t off_sflag;             // uint [128]   (their ids)
+  int32_t off_r0;                // int [128]    (their insertion points in the list)
+  int32_t off_S;                 // int [128] insertion points of the surviving pairs, ascending
+  int32_t off_fsrc;              // int [128] thread slot of the j-th survivor
+  int32_t off_misc;              // int [80] block scalars
 };
 
 struct SearchParams {

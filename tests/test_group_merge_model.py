@@ -1,0 +1,181 @@
+"""The group merge's algebra, checked on the CPU.
+
+The block kernel merges the two records of a pipe group into the candidate
+list in one pass (``merge_group`` in ``quiver-ae_b200/csrc/search_block.cuh``):
+survivors are ranked once over both records, and both lanes' picks are
+computed from insertion points before anything moves.  This file restates
+those formulas in Python, step for step, and checks them against the
+reference's order -- merge the first record, pick, merge the second, pick
+(``kernel_helpers.cuh:293-356`` merge, ``:456-473`` select) -- on random lists
+with tied distances, repeated ids within and across records, entries cut by
+ef and lists of every fill.  The kernel itself is held to the oracle bit for
+bit by the GPU tests; this test pins the reasoning that lets one pass stand
+for two.
+"""
+import bisect
+import random
+
+import pytest
+
+def seq_merge(L, pairs, ef):
+    # L: list of (d, id, visited) sorted; pairs: list of (d, id)
+    ids = {x[1] for x in L}
+    seen = set()
+    new = []
+    for d, i in pairs:
+        if i in ids or i in seen:
+            continue
+        seen.add(i)
+        new.append((d, i, False))
+    U = sorted(L + new, key=lambda x: (x[0], x[1]))
+    return U[:ef]
+
+def seq_select(L):
+    for j, x in enumerate(L):
+        if not x[2]:
+            L[j] = (x[0], x[1], True)
+            return x[1]
+    return -1
+
+def sequential(L0, A, B, ef):
+    L1 = seq_merge(list(L0), A, ef)
+    s0 = seq_select(L1)
+    if B is None:
+        return L1, s0, None
+    L2 = seq_merge(L1, B, ef)
+    s1 = seq_select(L2)
+    return L2, s0, s1
+
+def combined(L0, h, A, B, ef, RP=64):
+    sz = len(L0)
+    slots = [None] * 128
+    for e, pr in enumerate(A):
+        slots[e] = pr
+    if B is not None:
+        for e, pr in enumerate(B):
+            slots[RP + e] = pr
+    gact = 1 if B is None else 2
+    keys = [(x[0], x[1]) for x in L0]
+    pre = {}
+    for t, pr in enumerate(slots):
+        if pr is None:
+            continue
+        d, i = pr
+        if sz == ef and not ((d, i) < keys[-1]):
+            continue
+        r = bisect.bisect_left(keys, (d, i))
+        if r < sz and L0[r][1] == i:
+            continue
+        pre[t] = (d, i, r)
+    npre = len(pre)
+    if npre > 32:
+        return None
+    lanes = sorted(pre)  # compact order = slot order
+    dd = [pre[t][0] for t in lanes]; ii = [pre[t][1] for t in lanes]; rr = [pre[t][2] for t in lanes]
+    n = len(lanes)
+    lessm = [0] * n; eqm = [0] * n
+    for l in range(n):
+        for j in range(n):
+            if (dd[j], ii[j]) < (dd[l], ii[l]):
+                lessm[l] |= 1 << j
+            elif j < l and ii[j] == ii[l]:
+                eqm[l] |= 1 << j
+    valid = [eqm[l] == 0 for l in range(n)]
+    vm = sum(1 << l for l in range(n) if valid[l])
+    inA = [lanes[l] < RP for l in range(n)]
+    am = sum(1 << l for l in range(n) if valid[l] and inA[l])
+    rank = [bin(lessm[l] & vm).count('1') for l in range(n)]
+    rankA = [bin(lessm[l] & am).count('1') for l in range(n)]
+    S = [None] * 128; fsrc = [None] * 128
+    for l in range(n):
+        if valid[l]:
+            S[rank[l]] = rr[l]; fsrc[rank[l]] = lanes[l]
+    unv = [j for j in range(sz) if j >= h and not L0[j][2]]
+    NONE = 1 << 40
+    fu1 = unv[0] if len(unv) > 0 else NONE
+    fu2 = unv[1] if len(unv) > 1 else NONE
+    def count_all(i):
+        return sum(1 for l in range(n) if valid[l] and rr[l] <= i)
+    def find(pred):
+        c = [l for l in range(n) if pred(l)]
+        return c[0] if c else -1
+    lA = find(lambda l: valid[l] and inA[l] and rankA[l] == 0)
+    l0 = find(lambda l: valid[l] and rank[l] == 0)
+    l1 = find(lambda l: valid[l] and rank[l] == 1)
+    cf1 = count_all(fu1) if fu1 != NONE else 0
+    cf2 = count_all(fu2) if fu2 != NONE else 0
+    sel0 = -1; id0 = -1; pos0 = -1
+    if lA >= 0 and (fu1 == NONE or rr[lA] <= fu1):
+        sel0 = 0; id0 = ii[lA]; pos0 = rr[lA] + rank[lA]
+    elif fu1 != NONE:
+        sel0 = 1; id0 = L0[fu1][1]; pos0 = fu1 + cf1
+    id1 = -1; pos1 = -1
+    if gact == 2:
+        ls = l1 if (sel0 == 0 and l0 == lA) else l0
+        lo = fu2 if sel0 == 1 else fu1
+        if ls >= 0 and (lo == NONE or rr[ls] <= lo):
+            pos1 = rr[ls] + rank[ls]; id1 = ii[ls]
+        elif lo != NONE:
+            pos1 = lo + (cf1 if lo == fu1 else cf2); id1 = L0[lo][1]
+        if pos1 >= ef:
+            pos1 = -1; id1 = -1
+    if pos0 >= ef:
+        pos0 = -1
+    ns = bin(vm).count('1')
+    nsize = min(sz + ns, ef)
+    hint = (pos1 + 1 if id1 >= 0 else nsize) if gact == 2 else (pos0 + 1 if id0 >= 0 else nsize)
+    # phase C
+    out = [None] * ef
+    first = S[0] if ns > 0 else NONE
+    for i in range(sz):
+        dst = i + sum(1 for j in range(ns) if S[j] <= i) if i >= first else i
+        mark = dst == pos0 or dst == pos1
+        if dst < ef:
+            out[dst] = (L0[i][0], L0[i][1], L0[i][2] or mark)
+    for j in range(ns):
+        fp = S[j] + j
+        if fp < ef:
+            src = fsrc[j]
+            mark = fp == pos0 or fp == pos1
+            out[fp] = (slots[src][0], slots[src][1], mark)
+    out = out[:nsize]
+    assert all(x is not None for x in out), out
+    return out, id0, (id1 if gact == 2 else None), hint
+
+def rand_case(rng):
+    ef = rng.choice([4, 8, 16, 32, 64])
+    universe = rng.randint(ef, 4 * ef + 10)
+    dist = {i: float(rng.randint(0, universe // 2)) for i in range(universe)}  # ties in d
+    sz = rng.randint(0, ef)
+    L0ids = rng.sample(range(universe), sz)
+    L0 = sorted([(dist[i], i, False) for i in L0ids], key=lambda x: (x[0], x[1]))
+    # visited: random, with hint h: entries before h visited
+    h = rng.randint(0, sz)
+    L0 = [(x[0], x[1], True if j < h else rng.random() < 0.4) for j, x in enumerate(L0)]
+    def rec():
+        deg = rng.randint(0, 12)
+        ids = [rng.randrange(universe) for _ in range(deg)]
+        return [(dist[i], i) for i in ids]
+    A = rec()
+    B = rec() if rng.random() < 0.8 else None
+    return L0, h, A, B, ef
+
+
+@pytest.mark.parametrize("seed", [1, 2, 3])
+def test_group_merge_equals_two_merges(seed):
+    rng = random.Random(seed)
+    n_cmp = 0
+    for _ in range(6000):
+        L0, h, A, B, ef = rand_case(rng)
+        c = combined(L0, h, A, B, ef)
+        if c is None:
+            continue
+        out, id0, id1, hint = c
+        L, s0, s1 = sequential(L0, A, B, ef)
+        assert out == L
+        assert id0 == s0
+        if B is not None:
+            assert id1 == s1
+        assert hint <= len(out) and all(x[2] for x in out[:hint])
+        n_cmp += 1
+    assert n_cmp > 5000
