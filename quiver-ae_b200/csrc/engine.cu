@@ -164,7 +164,7 @@ Plan make_plan(qv_engine* e, const qv_search_opts& o, int64_t nq) {
   y.off_rid = take(int64_t(o.topk) * 4);
   y.off_rdist = take(int64_t(o.topk) * 4);
   y.rec_stride = static_cast<int32_t>(round_up(L.data_size, 16));
-  y.off_rec = take(int64_t(G) * y.rec_stride);
+  if (!pl.block) y.off_rec = take(int64_t(G) * y.rec_stride);  // the block kernel reads vectors in place
   y.off_lane = take(qvk::kMaxPipeWidth * 4);
   y.bytes = static_cast<int32_t>(round_up(off, 16));
   if (y.bytes > e->max_smem_optin)

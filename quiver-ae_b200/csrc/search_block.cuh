@@ -68,6 +68,7 @@ enum : int {
   kMiscGId0 = 64,   // first record's pick (-1: none)
   kMiscGId1 = 65,   // second record's pick (-1: none)
   kMiscGHint = 66,  // hint after the merge
+  kMiscDx = 67,     // [2] exact distance of each record's node (float bits)
   kMiscSlots = 80,
 };
 
@@ -83,7 +84,6 @@ struct BSlot {
   int* fsrc;        // [128] thread slot of the j-th survivor
   int32_t* rid;
   float* rdist;
-  uint8_t* rec;
   int32_t* lane;
   int* misc;
 };
@@ -101,7 +101,6 @@ __device__ __forceinline__ BSlot make_bslot(uint8_t* base, const SlotLayout& L) 
   s.fsrc = reinterpret_cast<int*>(base + L.off_fsrc);
   s.rid = reinterpret_cast<int32_t*>(base + L.off_rid);
   s.rdist = reinterpret_cast<float*>(base + L.off_rdist);
-  s.rec = base + L.off_rec;
   s.lane = reinterpret_cast<int32_t*>(base + L.off_lane);
   s.misc = reinterpret_cast<int*>(base + L.off_misc);
   return s;
@@ -161,6 +160,56 @@ __device__ __forceinline__ void build_lut_block(const SearchParams& p, const flo
   __syncthreads();
 }
 
+// Node v's record in the page store (ids are below 2^31, so 32-bit division).
+__device__ __forceinline__ const uint8_t* record_ptr(const SearchParams& p, uint32_t v) {
+  const uint32_t npp = static_cast<uint32_t>(p.npp);
+  return p.pages + static_cast<size_t>(v / npp) * kPageSize + static_cast<size_t>(v % npp) * p.node_size;
+}
+
+// The last warp of each active group scores the group's node exactly
+// (square_sum_32 order: lane l accumulates dims l, l + 32, ... with fused
+// multiply-adds, then the shfl_down tree), lane 0 keeps the distance.  For
+// byte vectors of up to 128 dims the warp loaded the vector with the record
+// (vw = word `lane`), and the bytes of dim l + 32 j come from word
+// l / 4 + 8 j by shuffle; otherwise the vector is read from the page store.
+template <typename T, int RP>
+__device__ __forceinline__ bool dx_warp(bool mine) {
+  return mine && ((threadIdx.x >> 5) + 1) % (RP / 32) == 0;
+}
+
+template <typename T>
+__device__ __forceinline__ bool dx_from_word(const SearchParams& p) {
+  return sizeof(T) == 1 && p.dim <= 128;
+}
+
+template <typename T, int RP>
+__device__ __forceinline__ void exact_l2_group(const SearchParams& p, const BSlot& s, bool mine, int g,
+                                               const uint32_t* rec, uint32_t vw) {
+  const int lane = threadIdx.x & 31;
+  if (!dx_warp<T, RP>(mine)) return;
+  float dx;
+  if (dx_from_word<T>(p)) {
+    float acc = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t w = __shfl_sync(kFull, vw, (lane >> 2) + 8 * j);
+      const int i = lane + 32 * j;
+      if (i < p.dim) {
+        const uint32_t b = (w >> (8 * (lane & 3))) & 0xffu;
+        const float x = static_cast<float>(static_cast<T>(b));
+        const float diff = __fsub_rn(s.q2[i], x);
+        acc = __fmaf_rn(diff, diff, acc);
+      }
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) acc = __fadd_rn(acc, __shfl_down_sync(kFull, acc, off));
+    dx = __shfl_sync(kFull, acc, 0);
+  } else {
+    dx = exact_l2_warp<T>(s.q2, reinterpret_cast<const T*>(rec), p.dim, lane);
+  }
+  if (lane == 0) s.misc[kMiscDx + g] = __float_as_int(dx);
+}
+
 // Warp 0: first unvisited entry at or after the hint; marks it, advances the
 // hint and stores the result in lane[w] (-1 instead when the query stopped).
 __device__ __forceinline__ void select_block_warp(const BSlot& s, int w, int lane) {
@@ -190,14 +239,12 @@ __device__ __forceinline__ void select_block_warp(const BSlot& s, int w, int lan
   __syncwarp();
 }
 
-// One warp: exact distance of the expanded node into the top-k, then the
-// step count and gpruning (kernel_q1.cuh:524-545) on its lane 0.  The
-// per-query counters live in misc[] because the visiting warp changes with
-// the record.
-template <typename T>
-__device__ __forceinline__ void visit_warp(const SearchParams& p, const BSlot& s, int gg, int node, int deg,
+// One warp: the expanded node's exact distance dx (computed while its record
+// was fetched) into the top-k, then the step count and gpruning
+// (kernel_q1.cuh:524-545) on its lane 0.  The per-query counters live in
+// misc[] because the visiting warp changes with the record.
+__device__ __forceinline__ void visit_warp(const SearchParams& p, const BSlot& s, float dx, int node, int deg,
                                            int lane) {
-  const float dx = exact_l2_warp<T>(s.q2, reinterpret_cast<const T*>(s.rec + gg * p.lay.rec_stride), p.dim, lane);
   int fc = s.misc[kMiscFc];
   if (fc < p.k || dx < s.rdist[p.k - 1]) {
     fc = topk_insert_warp(s.rid, s.rdist, fc, p.k, dx, node, lane);
@@ -286,7 +333,7 @@ __device__ __forceinline__ void merge_visit_select(const SearchParams& p, const 
     s.misc[kMiscMask + warp] = static_cast<int>(bal);
     s.misc[kMiscFu + warp] = fu;
   }
-  if (warp == vwarp) visit_warp<T>(p, s, gg, node, deg, lane);
+  if (warp == vwarp) visit_warp(p, s, __int_as_float(s.misc[kMiscDx + gg]), node, deg, lane);
   __syncthreads();
 
   // Phase B: survivors rank themselves among the survivors (ties, which only
@@ -645,12 +692,12 @@ __device__ __forceinline__ bool merge_group(const SearchParams& p, const BSlot& 
       s.misc[kMiscGHint] = gact == 2 ? (id1 >= 0 ? pos1 + 1 : nsize) : (id0 >= 0 ? pos0 + 1 : nsize);
     }
   } else if (warp == 1) {
-    visit_warp<T>(p, s, 0, s.misc[kMiscNode], s.misc[kMiscDeg], lane);
+    visit_warp(p, s, __int_as_float(s.misc[kMiscDx]), s.misc[kMiscNode], s.misc[kMiscDeg], lane);
     __syncwarp();
     if (lane == 0) s.misc[kMiscGStop0] = s.misc[kMiscStop];
     if (gact == 2) {
       __syncwarp();
-      visit_warp<T>(p, s, 1, s.misc[kMiscNode + 1], s.misc[kMiscDeg + 1], lane);
+      visit_warp(p, s, __int_as_float(s.misc[kMiscDx + 1]), s.misc[kMiscNode + 1], s.misc[kMiscDeg + 1], lane);
     }
   }
   __syncthreads();
@@ -716,14 +763,14 @@ __device__ int expand_block(const SearchParams& p, const BSlot& s, uint32_t mask
     const bool mine = g < gact;
     int64_t node = 0;
     uint32_t deg = 0, nb = 0;
+    const uint32_t* rec = nullptr;
+    uint32_t vw = 0;
     if (mine) {
       node = s.lane[ws[g]];
-      const uint32_t* rec = reinterpret_cast<const uint32_t*>(p.pages + (node / p.npp) * kPageSize +
-                                                              (node % p.npp) * p.node_size);
+      rec = reinterpret_cast<const uint32_t*>(record_ptr(p, static_cast<uint32_t>(node)));
       deg = rec[p.data_words];
       if (e < p.R) nb = rec[p.data_words + 1 + e];
-      uint32_t* dst = reinterpret_cast<uint32_t*>(s.rec + g * p.lay.rec_stride);
-      for (int i = e; i < p.data_words; i += RP) dst[i] = rec[i];
+      if (dx_warp<T, RP>(mine) && dx_from_word<T>(p) && (tid & 31) < p.data_words) vw = rec[tid & 31];
       if (e == 0) {
         s.misc[kMiscDeg + g] = static_cast<int>(deg);
         s.misc[kMiscNode + g] = static_cast<int>(node);
@@ -744,12 +791,16 @@ __device__ int expand_block(const SearchParams& p, const BSlot& s, uint32_t mask
         const uint4* src = reinterpret_cast<const uint4*>(p.codes + static_cast<int64_t>(nb) * MC);
 #pragma unroll
         for (int v = 0; v < NV; ++v) cw[v] = __ldg(src + v);
+      }
+      exact_l2_group<T, RP>(p, s, mine, g, rec, vw);  // while the code loads are in flight
+      if (live && !bad_nb) {
         float acc = 0.f;
 #pragma unroll
         for (int j = 0; j < MC; ++j) acc = __fadd_rn(acc, s.lut[j * kPivots + code_byte(cw[j >> 4], j & 15)]);
         d = acc;
       }
     } else {
+      exact_l2_group<T, RP>(p, s, mine, g, rec, vw);
       if (live && !bad_nb) {
         const uint8_t* src = p.codes + static_cast<int64_t>(nb) * p.M;
         float acc = 0.f;
