@@ -155,6 +155,7 @@ Plan make_plan(qv_engine* e, const qv_search_opts& o, int64_t nq) {
     y.off_S = take(qvk::kBlock * 4);
     y.off_fsrc = take(qvk::kBlock * 4);
     y.off_misc = take(qvk::kMiscSlots * 4);
+    y.off_sort = take(2 * 3 * qvk::kBlock * 4);
   } else {
     y.off_nid = take(rp * 4);
     y.off_ndist = take(rp * 4);

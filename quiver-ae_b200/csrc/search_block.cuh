@@ -69,6 +69,7 @@ enum : int {
   kMiscGId1 = 65,   // second record's pick (-1: none)
   kMiscGHint = 66,  // hint after the merge
   kMiscDx = 67,     // [2] exact distance of each record's node (float bits)
+  kMiscGRep = 72,   // [4] many-pair merge: sorted positions of pairs repeating an id
   kMiscSlots = 80,
 };
 
@@ -86,6 +87,7 @@ struct BSlot {
   float* rdist;
   int32_t* lane;
   int* misc;
+  uint32_t* sortbuf;  // [2][3][128] many-pair sort exchange buffers
 };
 
 __device__ __forceinline__ BSlot make_bslot(uint8_t* base, const SlotLayout& L) {
@@ -103,6 +105,7 @@ __device__ __forceinline__ BSlot make_bslot(uint8_t* base, const SlotLayout& L) 
   s.rdist = reinterpret_cast<float*>(base + L.off_rdist);
   s.lane = reinterpret_cast<int32_t*>(base + L.off_lane);
   s.misc = reinterpret_cast<int*>(base + L.off_misc);
+  s.sortbuf = reinterpret_cast<uint32_t*>(base + L.off_sort);
   return s;
 }
 
@@ -507,6 +510,218 @@ __device__ __forceinline__ int nth_set_bit(unsigned m, int n) {
   return pos;
 }
 
+// Many-pair ranking for merge_group (more than 32 surviving pairs): a
+// bitonic sort of the group's 128 slots by (dist, id, record, slot), pairs
+// that cannot enter the list last.  Strides below 32 exchange by shuffle,
+// the three of 32 and 64 through shared memory (two buffers, so one barrier
+// each).  The records' order puts the first record's copy of an id first,
+// and a sorted pair whose predecessor has its id drops out; the others
+// compact themselves by the count of dropped pairs before them (a bitmask
+// over sorted positions) and store their insertion point and slot at their
+// rank in S / fsrc, as the small path does.  Ends with a barrier; the
+// survivor count goes to kMiscGNs.
+template <int RP>
+__device__ __forceinline__ void merge_group_many_rank(const BSlot& s, int npre, bool pre, float d, uint32_t id) {
+  const int tid = threadIdx.x;
+  uint32_t khi = pre ? __float_as_uint(d) : 0xffffffffu;
+  uint32_t klo = pre ? (((id & kIdMask) << 1) | (tid >= RP ? 1u : 0u)) : 0xffffffffu;
+  uint32_t slot = static_cast<uint32_t>(tid);
+  int buf = 0;
+#pragma unroll
+  for (int k = 2; k <= kBlock; k <<= 1) {
+#pragma unroll
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      const int partner = tid ^ j;
+      uint32_t ohi, olo, osl;
+      if (j >= 32) {
+        uint32_t* b = s.sortbuf + buf * 3 * kBlock;
+        b[tid] = khi;
+        b[kBlock + tid] = klo;
+        b[2 * kBlock + tid] = slot;
+        __syncthreads();
+        ohi = b[partner];
+        olo = b[kBlock + partner];
+        osl = b[2 * kBlock + partner];
+        buf ^= 1;
+      } else {
+        ohi = __shfl_xor_sync(kFull, khi, j);
+        olo = __shfl_xor_sync(kFull, klo, j);
+        osl = __shfl_xor_sync(kFull, slot, j);
+      }
+      const bool mine_less = khi < ohi || (khi == ohi && (klo < olo || (klo == olo && slot < osl)));
+      const bool want_min = ((tid & k) == 0) == (tid < partner);
+      if (mine_less != want_min) {
+        khi = ohi;
+        klo = olo;
+        slot = osl;
+      }
+    }
+  }
+  // sorted: position tid holds (khi, klo, slot); the first npre are pairs
+  uint32_t* b = s.sortbuf + buf * 3 * kBlock;
+  b[tid] = khi;
+  b[kBlock + tid] = klo;
+  __syncthreads();
+  const bool rep = tid > 0 && tid < npre && b[tid - 1] == khi && (b[kBlock + tid - 1] >> 1) == (klo >> 1);
+  if (rep) atomicOr(reinterpret_cast<unsigned*>(&s.misc[kMiscGRep + (tid >> 5)]), 1u << (tid & 31));
+  __syncthreads();
+  int nrep = 0, before = 0;
+#pragma unroll
+  for (int x = 0; x < 4; ++x) {
+    const unsigned rx = static_cast<unsigned>(s.misc[kMiscGRep + x]);
+    const int w = tid >> 5;
+    nrep += __popc(rx);
+    before += x < w ? __popc(rx) : (x == w ? __popc(rx & ((1u << (tid & 31)) - 1u)) : 0);
+  }
+  if (tid < npre && !rep) {
+    const int rank = tid - before;
+    s.S[rank] = s.r0[slot];
+    s.fsrc[rank] = static_cast<int>(slot);
+  }
+  if (tid == 0) s.misc[kMiscGNs] = npre - nrep;
+  __syncthreads();
+}
+
+// Warp 0, many-pair path: both lanes' picks from the sorted survivors
+// (S = insertion points, fsrc = slots, ascending by key), with the same rules
+// as the small path; writes the same block scalars.
+template <int RP>
+__device__ __forceinline__ void merge_group_picks_sorted(const SearchParams& p, const BSlot& s, int gact, int sz) {
+  const int lane = threadIdx.x & 31;
+  const int ef = p.ef;
+  constexpr int kNone = 0x7fffffff;
+  const int ns = s.misc[kMiscGNs];
+  const int a = lane < 4 ? s.misc[kMiscGFu1 + lane] : kNone;
+  const int b = lane < 4 ? s.misc[kMiscGFu2 + lane] : kNone;
+  const int fu1 = __reduce_min_sync(kFull, a);
+  const int fu2 = __reduce_min_sync(kFull, a == fu1 ? b : a);
+  // the first survivor from the group's first record
+  int lA = -1;
+  for (int b0 = 0; b0 < ns && lA < 0; b0 += 32) {
+    const int j = b0 + lane;
+    const unsigned fa = __ballot_sync(kFull, j < ns && s.fsrc[j] < RP);
+    if (fa) lA = b0 + __ffs(fa) - 1;
+  }
+  int sel0 = -1, id0 = -1, pos0 = -1;
+  if (lA >= 0 && (fu1 == kNone || s.S[lA] <= fu1)) {
+    sel0 = 0;
+    id0 = static_cast<int>(s.si[s.fsrc[lA]] & kIdMask);
+    pos0 = s.S[lA] + lA;
+  } else if (fu1 != kNone) {
+    sel0 = 1;
+    id0 = static_cast<int>(s.lid[fu1] & kIdMask);
+    pos0 = fu1 + count_le(s.S, ns, fu1);
+  }
+  int id1 = -1, pos1 = -1;
+  if (gact == 2) {
+    const int ls = (sel0 == 0 && lA == 0) ? 1 : 0;
+    const int lo = sel0 == 1 ? fu2 : fu1;
+    if (ls < ns && (lo == kNone || s.S[ls] <= lo)) {
+      pos1 = s.S[ls] + ls;
+      id1 = static_cast<int>(s.si[s.fsrc[ls]] & kIdMask);
+    } else if (lo != kNone) {
+      pos1 = lo + count_le(s.S, ns, lo);
+      id1 = static_cast<int>(s.lid[lo] & kIdMask);
+    }
+    if (pos1 >= ef) { pos1 = -1; id1 = -1; }
+  }
+  if (pos0 >= ef) pos0 = -1;
+  if (lane == 0) {
+    const int nsize = min(sz + ns, ef);
+    s.misc[kMiscGPos0] = pos0;
+    s.misc[kMiscGPos1] = pos1;
+    s.misc[kMiscGId0] = id0;
+    s.misc[kMiscGId1] = id1;
+    s.misc[kMiscGHint] = gact == 2 ? (id1 >= 0 ? pos1 + 1 : nsize) : (id0 >= 0 ? pos0 + 1 : nsize);
+  }
+}
+
+// Last phase of merge_group: old entries at or after the first insertion
+// point move up by the number of insertion points at or below them
+// (lc: this thread's entries tid, tid + 128, ... read before anything
+// moved), survivors land at insertion point + rank, entries pushed past ef
+// are dropped, the writers of the two picks set their visited bits, and
+// thread 0 stores the size, the hint and the lanes' next nodes.
+struct ListCopy {
+  uint32_t id[kFastEntries];
+  float d[kFastEntries];
+};
+
+__device__ __forceinline__ void merge_group_write(const SearchParams& p, const BSlot& s, int gact, int sz,
+                                                  const ListCopy lc) {
+  const int tid = threadIdx.x;
+  const int ef = p.ef;
+  const int ns = s.misc[kMiscGNs];
+  const int pos0 = s.misc[kMiscGPos0];
+  const int pos1 = s.misc[kMiscGPos1];
+  const int first = ns > 0 ? s.S[0] : 0x7fffffff;
+#pragma unroll
+  for (int x = 0; x < kFastEntries; ++x) {
+    const int i = tid + kBlock * x;
+    if (i < sz) {
+      const int dst = i >= first ? i + count_le(s.S, ns, i) : i;
+      const bool mark = dst == pos0 || dst == pos1;
+      if (dst < ef && (dst != i || mark)) {
+        s.lid[dst] = lc.id[x] | (mark ? kVisited : 0u);
+        s.ldist[dst] = lc.d[x];
+      }
+    }
+  }
+  if (tid < ns) {
+    const int fp = s.S[tid] + tid;
+    const int src = s.fsrc[tid];
+    if (fp >= 0 && fp < ef && src >= 0 && src < kBlock) {
+      const bool mark = fp == pos0 || fp == pos1;
+      s.lid[fp] = s.si[src] | (mark ? kVisited : 0u);
+      s.ldist[fp] = s.sd[src];
+    }
+  }
+  if (tid == 0) {
+    s.misc[kMiscSize] = min(sz + ns, ef);
+    s.misc[kMiscHint] = s.misc[kMiscGHint];
+    const int id0 = s.misc[kMiscGId0];
+    s.lane[s.misc[kMiscWs]] = (id0 >= 0 && !s.misc[kMiscGStop0]) ? id0 : -1;
+    if (gact == 2) {
+      const int id1 = s.misc[kMiscGId1];
+      s.lane[s.misc[kMiscWs + 1]] = (id1 >= 0 && !s.misc[kMiscStop]) ? id1 : -1;
+    }
+  }
+  __syncthreads();
+}
+
+// Warp 1: visit the group's nodes in lane order, keeping the stop flag right
+// after the first visit for the first lane.
+__device__ __forceinline__ void merge_group_visits(const SearchParams& p, const BSlot& s, int gact, int lane) {
+  visit_warp(p, s, __int_as_float(s.misc[kMiscDx]), s.misc[kMiscNode], s.misc[kMiscDeg], lane);
+  __syncwarp();
+  if (lane == 0) s.misc[kMiscGStop0] = s.misc[kMiscStop];
+  if (gact == 2) {
+    __syncwarp();
+    visit_warp(p, s, __int_as_float(s.misc[kMiscDx + 1]), s.misc[kMiscNode + 1], s.misc[kMiscDeg + 1], lane);
+  }
+}
+
+// Many-pair path of merge_group: rank, read this thread's old entries (the
+// list does not move until the write phase), picks on warp 0 and visits on
+// warp 1, then the write phase.
+template <int RP>
+__device__ __forceinline__ void merge_group_many(const SearchParams& p, const BSlot& s, int gact, int sz, int npre,
+                                                 bool pre, float d, uint32_t id) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  merge_group_many_rank<RP>(s, npre, pre, d, id);
+  ListCopy lc;
+#pragma unroll
+  for (int x = 0; x < kFastEntries; ++x) {
+    const int i = tid + kBlock * x;
+    lc.id[x] = i < sz ? s.lid[i] : 0u;
+    lc.d[x] = i < sz ? s.ldist[i] : 0.f;
+  }
+  if (warp == 0) merge_group_picks_sorted<RP>(p, s, gact, sz);
+  if (warp == 1) merge_group_visits(p, s, gact, lane);
+  __syncthreads();
+  merge_group_write(p, s, gact, sz, lc);
+}
+
 // Merge the records of one group (one or two pipe lanes, in lane order) into
 // the list in a single pass, visit their nodes and pick each lane's next node.
 //
@@ -523,11 +738,11 @@ __device__ __forceinline__ int nth_set_bit(unsigned m, int n) {
 // union.  Both picks are computed from the insertion points below, before
 // anything moves.
 //
-// Returns false, having changed nothing, when more than 32 pairs survive the
-// filter (the opening hops of a query); the caller then merges the records
-// one by one.
+// When more than 32 pairs survive the filter (the opening hops of a query),
+// all threads rank them instead (merge_group_many_rank) and warp 0 takes the
+// picks from the sorted survivors.
 template <typename T, int RP>
-__device__ __forceinline__ bool merge_group(const SearchParams& p, const BSlot& s, int gact, bool live, float d,
+__device__ __forceinline__ void merge_group(const SearchParams& p, const BSlot& s, int gact, bool live, float d,
                                             uint32_t id) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int sz = s.misc[kMiscSize];
@@ -538,11 +753,12 @@ __device__ __forceinline__ bool merge_group(const SearchParams& p, const BSlot& 
   // pairs whose id is listed; old entries into registers; the first two
   // unvisited entries at or after the hint.
   bool pre = false;
+  int r = 0;
   if (live) {
     bool cand = true;
     if (sz == ef) cand = key_less(d, id, s.ldist[sz - 1], s.lid[sz - 1]);
     if (cand) {
-      const int r = lower_bound_s(s.ldist, s.lid, sz, d, id);
+      r = lower_bound_s(s.ldist, s.lid, sz, d, id);
       pre = !(r < sz && ((s.lid[r] ^ id) & kIdMask) == 0);
       if (pre) {
         s.sd[tid] = d;
@@ -575,6 +791,7 @@ __device__ __forceinline__ bool merge_group(const SearchParams& p, const BSlot& 
       s.misc[kMiscGMask + warp] = static_cast<int>(bal);
       s.misc[kMiscGFu1 + warp] = w1;
       s.misc[kMiscGFu2 + warp] = w2;
+      s.misc[kMiscGRep + warp] = 0;
     }
   }
   __syncthreads();
@@ -586,10 +803,12 @@ __device__ __forceinline__ bool merge_group(const SearchParams& p, const BSlot& 
     m[x] = static_cast<unsigned>(s.misc[kMiscGMask + x]);
     npre += __popc(m[x]);
   }
-  if (npre > 32) return false;  // uniform: every thread read the same ballots
-
   // Phase B: warp 0 ranks the surviving pairs and computes both picks; warp
   // 1 visits the records' nodes in lane order.
+  if (npre > 32) {  // uniform: every thread read the same ballots
+    merge_group_many<RP>(p, s, gact, sz, npre, pre, d, id);
+    return;
+  }
   if (warp == 0) {
     int slot = -1;
     float dd = 0.f;
@@ -692,54 +911,17 @@ __device__ __forceinline__ bool merge_group(const SearchParams& p, const BSlot& 
       s.misc[kMiscGHint] = gact == 2 ? (id1 >= 0 ? pos1 + 1 : nsize) : (id0 >= 0 ? pos0 + 1 : nsize);
     }
   } else if (warp == 1) {
-    visit_warp(p, s, __int_as_float(s.misc[kMiscDx]), s.misc[kMiscNode], s.misc[kMiscDeg], lane);
-    __syncwarp();
-    if (lane == 0) s.misc[kMiscGStop0] = s.misc[kMiscStop];
-    if (gact == 2) {
-      __syncwarp();
-      visit_warp(p, s, __int_as_float(s.misc[kMiscDx + 1]), s.misc[kMiscNode + 1], s.misc[kMiscDeg + 1], lane);
-    }
+    merge_group_visits(p, s, gact, lane);
   }
   __syncthreads();
 
-  // Phase C: shifted writes; the writers of the picks mark them.
-  const int ns = s.misc[kMiscGNs];
-  const int pos0 = s.misc[kMiscGPos0];
-  const int pos1 = s.misc[kMiscGPos1];
-  const int first = ns > 0 ? s.S[0] : 0x7fffffff;
+  ListCopy lc;
 #pragma unroll
   for (int x = 0; x < kFastEntries; ++x) {
-    const int i = tid + kBlock * x;
-    if (i < sz) {
-      const int dst = i >= first ? i + count_le(s.S, ns, i) : i;
-      const bool mark = dst == pos0 || dst == pos1;
-      if (dst < ef && (dst != i || mark)) {
-        s.lid[dst] = vid[x] | (mark ? kVisited : 0u);
-        s.ldist[dst] = vd[x];
-      }
-    }
+    lc.id[x] = vid[x];
+    lc.d[x] = vd[x];
   }
-  if (tid < ns) {
-    const int fp = s.S[tid] + tid;
-    if (fp >= 0 && fp < ef) {
-      const int src = s.fsrc[tid];
-      const bool mark = fp == pos0 || fp == pos1;
-      s.lid[fp] = s.si[src] | (mark ? kVisited : 0u);
-      s.ldist[fp] = s.sd[src];
-    }
-  }
-  if (tid == 0) {
-    s.misc[kMiscSize] = min(sz + ns, ef);
-    s.misc[kMiscHint] = s.misc[kMiscGHint];
-    const int id0 = s.misc[kMiscGId0];
-    s.lane[s.misc[kMiscWs]] = (id0 >= 0 && !s.misc[kMiscGStop0]) ? id0 : -1;
-    if (gact == 2) {
-      const int id1 = s.misc[kMiscGId1];
-      s.lane[s.misc[kMiscWs + 1]] = (id1 >= 0 && !s.misc[kMiscStop]) ? id1 : -1;
-    }
-  }
-  __syncthreads();
-  return true;
+  merge_group_write(p, s, gact, sz, lc);
 }
 
 // Expand the lanes in `mask`, in lane order, G = 128 / RP records at a time.
@@ -810,7 +992,10 @@ __device__ int expand_block(const SearchParams& p, const BSlot& s, uint32_t mask
     }
     __syncthreads();
     if (s.misc[kMiscErr]) return s.misc[kMiscErr];
-    if (p.ef <= kBlock * kFastEntries && merge_group<T, RP>(p, s, gact, live, d, nb)) continue;
+    if (p.ef <= kBlock * kFastEntries) {
+      merge_group<T, RP>(p, s, gact, live, d, nb);
+      continue;
+    }
     for (int gg = 0; gg < gact; ++gg) merge_visit_select<T, RP>(p, s, gg, g == gg, live, d, nb);
   }
   return 0;

@@ -59,6 +59,7 @@ struct SlotLayout {
   int32_t off_S;                 // int [128] insertion points of the surviving pairs, ascending
   int32_t off_fsrc;              // int [128] thread slot of the j-th survivor
   int32_t off_misc;              // int [80] block scalars
+  int32_t off_sort;              // uint [2][3][128] exchange buffers of the many-pair sort
 };
 
 struct SearchParams {
