@@ -217,6 +217,12 @@ def main() -> int:
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    # torchrun pins every rank to one OpenMP thread; the host-side work here
+    # (the index build on rank 0 while the other ranks wait, the reference
+    # arm on rank 0 alone) should use every core.  Set before any native
+    # library with OpenMP is loaded.
+    if "LOCAL_RANK" in os.environ and os.environ.get("OMP_NUM_THREADS") == "1":
+        os.environ["OMP_NUM_THREADS"] = str(os.cpu_count() or 1)
     if args.impl == "reference":
         return reference_arm(args, rank, world)
 
