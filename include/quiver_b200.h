@@ -109,6 +109,9 @@ typedef struct {
   int32_t gpruning_warmup_steps;  /* default 10 */
   int32_t gpruning_patience;      /* default 8 */
   int32_t lut_mode;               /* QV_LUT_FP32 */
+  int32_t skip_nav;               /* 1: start every query at the medoid even when the engine holds
+                                     a nav graph (the CLI's --skip-nav, bin/quiver_search.cu:118-122,
+                                     241-245); default 0 */
 } qv_search_opts;
 
 typedef struct {
@@ -137,6 +140,24 @@ int qv_engine_create(const qv_engine_opts* opts, qv_engine** out);
 int qv_engine_create_from_arrays(const qv_index_arrays* arrays, int32_t device,
                                  int32_t page_store, qv_engine** out);
 int qv_engine_info(const qv_engine* engine, qv_index_info* info);
+
+/* Navigation graph for the per-query entry search.  qv_engine_create loads
+ * one when the index directory (or its nav/ child) holds nav_index,
+ * nav_index.data and map.txt, as prepare_search_setup does
+ * (bin/common/search_setup.hpp:96-105 with NavGraph::init,
+ * src/shared/index/nav_graph.cu:12-73); every search then starts from the
+ * node the in-kernel entry search picks (src/quiver/kernel_core/
+ * inkernel_nav.cuh:60-201, called at kernel_q1.cuh:149-202) instead of the
+ * medoid, unless its options set skip_nav.
+ *
+ * qv_engine_set_nav replaces the engine's nav graph from host arrays:
+ * data = num_node vectors of the index's type and dim, graph = [num_node x
+ * max_m] nav ids padded with -1 (0 < max_m <= 32), mapping = nav id -> base
+ * id, start = the nav id the search begins at.  num_node == 0 removes it.
+ * qv_engine_nav_info reports num_node (0: none), max_m and start. */
+int qv_engine_set_nav(qv_engine* engine, const void* data, const int32_t* graph, const int32_t* mapping,
+                      int32_t num_node, int32_t max_m, int32_t start);
+int qv_engine_nav_info(const qv_engine* engine, int32_t* num_node, int32_t* max_m, int32_t* start);
 void qv_engine_destroy(qv_engine* engine);
 
 /* Search with HOST buffers: queries [nq x dim] fp32 (the reference's float

@@ -281,12 +281,117 @@ static int orc_gpruning(orc_gp* g, const orc_ctx* c, const orc_params* p) {
          g->cnt >= p->gpruning_patience;
 }
 
+
+/* ------------------------------------------------------------ nav entry -- */
+
+#define ORC_NAV_L 4   /* inkernel_nav.cuh:51 */
+#define ORC_NAV_R 28  /* inkernel_nav.cuh:52 */
+
+/* Neighbour i of nav node u as the reference reads it: graph[max_m * u + i]
+ * for i < 28 (inkernel_nav.cuh:113-119), so a row shorter than 28 runs on
+ * into the next row; past the array's end the row counts as ended. */
+static int32_t nav_edge(const orc_nav* nav, int32_t u, int i) {
+  const int64_t at = (int64_t)nav->max_m * u + i;
+  if (at >= (int64_t)nav->num_node * nav->max_m) return -1;
+  return nav->graph[at];
+}
+
+static float nav_dist(const orc_index* ix, const orc_nav* nav, const float* q, int32_t v) {
+  const int64_t elem = ix->data_type == ORC_FLOAT ? 4 : 1;
+  return orc_exact_l2(q, nav->data + (int64_t)v * ix->dim * elem, ix->dim, ix->data_type);
+}
+
+int64_t orc_nav_entry(const orc_index* ix, const orc_nav* nav, const float* q) {
+  const int L = ORC_NAV_L, R = ORC_NAV_R;
+  uint32_t pid[32];
+  float pd[32];
+  if (nav->start < 0 || nav->start >= nav->num_node) return -20;
+  /* 82-94: the start node in slot 0, empty slots */
+  pid[0] = (uint32_t)nav->start;
+  pd[0] = nav_dist(ix, nav, q, nav->start);
+  for (int l = 1; l < L + R; ++l) { pid[l] = 0xffffffffu; pd[l] = INFINITY; }
+  int idx = 0;
+  /* the four best only improve, so the walk ends; the cap is a safety net */
+  const int64_t cap = 4 * (int64_t)nav->num_node + 64;
+  for (int64_t hop = 0; idx != -1; ++hop) {
+    if (hop > cap) return -21;
+    const int32_t u = (int32_t)(pid[idx] & ORC_IDMASK);
+    if (u >= nav->num_node) return -22;
+    pid[idx] |= ORC_VISITED;                                  /* 101-104 */
+    /* 113-135: four warps take 7 neighbour slots each; a warp stops at its
+     * first -1, leaving its remaining slots as they were */
+    for (int w = 0; w < 4; ++w) {
+      for (int i = 7 * w; i < 7 * w + 7 && i < R; ++i) {
+        const int32_t v = nav_edge(nav, u, i);
+        if (v == -1) break;
+        if (v < 0 || v >= nav->num_node) return -22;
+        pid[i + L] = (uint32_t)v;
+        pd[i + L] = nav_dist(ix, nav, q, v);
+      }
+    }
+    /* 142-182: four rounds; round i moves the smallest remaining slot to i */
+    for (int i = 0; i < L; ++i) {
+      float dist[32];
+      int pos[32];
+      int dupl[32];
+      for (int l = 0; l < 32; ++l) {
+        dist[l] = pd[l];
+        pos[l] = l;
+        dupl[l] = 0;
+        if (l < i) dist[l] = INFINITY;
+        else if (i != 0 && ((pid[l] ^ pid[i - 1]) & ORC_IDMASK) == 0) dupl[l] = 1;
+      }
+      /* a copy of the previous round's pick gives it its visited bit and
+       * leaves the race (the reference ORs from several lanes at once; here
+       * every copy's bit is kept) */
+      for (int l = 0; l < 32; ++l) {
+        if (!dupl[l]) continue;
+        pid[i - 1] |= pid[l];
+        pd[l] = INFINITY;
+        dist[l] = INFINITY;
+      }
+      /* 159-167: shfl_down argmin tree; a value replaces only a strictly
+       * larger one, and a lane past 31 reads its own value */
+      for (int off = 16; off > 0; off >>= 1) {
+        float nd[32];
+        int np[32];
+        for (int l = 0; l < 32; ++l) {
+          const int src = l + off < 32 ? l + off : l;
+          nd[l] = dist[l];
+          np[l] = pos[l];
+          if (dist[src] < dist[l]) { nd[l] = dist[src]; np[l] = pos[src]; }
+        }
+        memcpy(dist, nd, sizeof(dist));
+        memcpy(pos, np, sizeof(pos));
+      }
+      const int p0 = pos[0];
+      if (i != p0) {                                            /* 170-180 */
+        const float t = pd[i], y = pd[p0];
+        if (t != y) {
+          pd[i] = y; pd[p0] = t;
+          const uint32_t m = pid[i]; pid[i] = pid[p0]; pid[p0] = m;
+        }
+      }
+    }
+    /* 186-191: the first unvisited slot, if it is one of the first four */
+    idx = -1;
+    for (int l = 0; l < 32; ++l) {
+      if (!(pid[l] & ORC_VISITED)) { idx = l < L ? l : -1; break; }
+    }
+  }
+  const uint32_t raw = pid[0] & ORC_IDMASK;                   /* 199-200 */
+  if (raw >= (uint32_t)nav->num_node) return -23;
+  const int32_t entry = nav->mapping[raw];
+  if (entry < 0 || entry >= ix->num_points) return -24;
+  return entry;
+}
+
 /* ------------------------------------------------------------- search -- */
 
 /* One query, kernel_q1.cuh:180-704 with every issued lane completing before
  * the next poll: each pipe iteration expands the active lanes in lane order
  * (489-600), then refills the lanes that were idle (619-630). */
-static int orc_search_one(const orc_index* ix, orc_ctx* c, const float* q,
+static int orc_search_one(const orc_index* ix, const orc_nav* nav, orc_ctx* c, const float* q,
                           const orc_params* p, int32_t* lane_req, int* out_steps) {
   const int ef = p->ef_search, k = p->topk, W = p->pipe_width;
   const int early = p->early_exit_policy != ORC_EXIT_NONE;
@@ -298,7 +403,13 @@ static int orc_search_one(const orc_index* ix, orc_ctx* c, const float* q,
   for (int w = 0; w < W; ++w) lane_req[w] = -1;
 
   orc_gp g = {0, 0, 0, INFINITY, INFINITY};
-  const int64_t entry = ix->medoid;               /* 199-206, no nav graph */
+  /* 149-202: the nav result when a nav graph is loaded, else the medoid;
+   * nav reads the query before the centroid round trip */
+  int64_t entry = ix->medoid;
+  if (nav) {
+    entry = orc_nav_entry(ix, nav, q);
+    if (entry < 0) return (int)entry;
+  }
   int rc = orc_merge(ix, c, entry, ef);
   if (rc) return rc;
   lane_req[0] = orc_visit_select(ix, c, entry, ef, k);
@@ -335,6 +446,12 @@ static int orc_search_one(const orc_index* ix, orc_ctx* c, const float* q,
 int orc_search(const orc_index* ix, const float* queries, int64_t nq,
                const orc_params* p, int32_t* ids, float* dists,
                int32_t* found, int32_t* steps, int64_t* nbrs) {
+  return orc_search_nav(ix, NULL, queries, nq, p, ids, dists, found, steps, nbrs);
+}
+
+int orc_search_nav(const orc_index* ix, const orc_nav* nav, const float* queries, int64_t nq,
+                   const orc_params* p, int32_t* ids, float* dists,
+                   int32_t* found, int32_t* steps, int64_t* nbrs) {
   if (p->topk <= 0 || p->ef_search <= 0 || p->pipe_width <= 0 || p->pipe_width > 64)
     return -10;
   int err = 0;
@@ -364,7 +481,7 @@ int orc_search(const orc_index* ix, const float* queries, int64_t nq,
 #endif
     for (int64_t qi = 0; qi < nq; ++qi) {
       int st = 0;
-      const int rc = orc_search_one(ix, &c, queries + qi * ix->dim, p, lane_req, &st);
+      const int rc = orc_search_one(ix, nav, &c, queries + qi * ix->dim, p, lane_req, &st);
       if (rc) {
 #ifdef _OPENMP
 #pragma omp critical

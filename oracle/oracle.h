@@ -17,6 +17,8 @@
  *   select without compaction   src/quiver/kernel_core/kernel_helpers.cuh:491-518
  *   hop loop, W lanes, gpruning src/quiver/kernel_core/kernel_q1.cuh:199-425,489-654
  *   page addressing             src/quiver/search.cu:240, kernel_helpers.cuh:257
+ *   nav entry search            src/quiver/kernel_core/inkernel_nav.cuh:60-201,
+ *                               used by kernel_q1.cuh:149-202; files nav_graph.cu:12-73
  *
  * Floating point: fp32 round-to-nearest, fused multiply-add exactly where the
  * reference writes `acc += d * d` (nvcc's default --fmad=true contracts it),
@@ -62,6 +64,22 @@ typedef struct {
   int32_t num_threads;          /* OpenMP threads for orc_search; <=0 means all */
 } orc_params;
 
+/* A navigation graph (src/shared/index/nav_graph.cu:12-73).  Vectors have
+ * the base set's data type and dim. */
+typedef struct {
+  const uint8_t* data;     /* num_node * dim elements */
+  const int32_t* graph;    /* num_node * max_m, -1 padded */
+  const int32_t* mapping;  /* num_node: nav id -> base id */
+  int32_t num_node;
+  int32_t max_m;           /* <= 32 */
+  int32_t start;
+} orc_nav;
+
+/* The in-kernel entry search for one query on its ORIGINAL vector (before
+ * the centroid round trip), inkernel_nav.cuh:60-201: returns the base id
+ * of the best nav node, or a negative code on a malformed nav graph. */
+int64_t orc_nav_entry(const orc_index* ix, const orc_nav* nav, const float* query);
+
 /* LUT [M x 256] and q'' [dim] for one query (pq_device.cuh:9-36). */
 void orc_build_lut(const orc_index* ix, const float* query, float* lut, float* q2);
 
@@ -78,6 +96,12 @@ float orc_exact_l2(const float* q2, const void* vec, int64_t dim, int32_t dtype)
 int orc_search(const orc_index* ix, const float* queries, int64_t nq,
                const orc_params* p, int32_t* ids, float* dists,
                int32_t* found, int32_t* steps, int64_t* nbrs);
+
+/* orc_search with each query's entry from the nav graph (nav may be NULL:
+ * entry = medoid, as orc_search). */
+int orc_search_nav(const orc_index* ix, const orc_nav* nav, const float* queries, int64_t nq,
+                   const orc_params* p, int32_t* ids, float* dists,
+                   int32_t* found, int32_t* steps, int64_t* nbrs);
 
 /* Recall@k as bin/common/recall.hpp:44-62 defines it. */
 double orc_calc_recall(const int32_t* results, const int32_t* gt,

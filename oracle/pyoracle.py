@@ -58,6 +58,11 @@ class _Params(C.Structure):
 _lib = None
 
 
+class _Nav(C.Structure):
+    _fields_ = [("data", C.c_void_p), ("graph", C.c_void_p), ("mapping", C.c_void_p), ("num_node", C.c_int32),
+                ("max_m", C.c_int32), ("start", C.c_int32)]
+
+
 def lib() -> C.CDLL:
     global _lib
     if _lib is None:
@@ -71,6 +76,11 @@ def lib() -> C.CDLL:
         _lib.orc_search.argtypes = [C.POINTER(_Index), C.c_void_p, C.c_int64, C.POINTER(_Params), C.c_void_p,
                                     C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]
         _lib.orc_search.restype = C.c_int
+        _lib.orc_search_nav.argtypes = [C.POINTER(_Index), C.c_void_p, C.c_void_p, C.c_int64, C.POINTER(_Params),
+                                        C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]
+        _lib.orc_search_nav.restype = C.c_int
+        _lib.orc_nav_entry.argtypes = [C.POINTER(_Index), C.POINTER(_Nav), C.c_void_p]
+        _lib.orc_nav_entry.restype = C.c_int64
         _lib.orc_calc_recall.argtypes = [C.c_void_p, C.c_void_p, C.c_int64, C.c_int64, C.c_int32]
         _lib.orc_calc_recall.restype = C.c_double
     return _lib
@@ -156,6 +166,52 @@ def load_index(index_dir: str | Path, data_type: str) -> OracleIndex:
                        np.ascontiguousarray(chunk_offsets, dtype=np.int32))
 
 
+@dataclass
+class OracleNav:
+    """A navigation graph as NavGraph::init (src/shared/index/nav_graph.cu:12-73) reads it."""
+    data: np.ndarray     # [num_node, dim], base data type
+    graph: np.ndarray    # [num_node, max_m] i32, -1 padded
+    mapping: np.ndarray  # [num_node] i32
+    start: int
+    max_m: int
+
+    def __post_init__(self):
+        self._c = _Nav(self.data.ctypes.data, self.graph.ctypes.data, self.mapping.ctypes.data,
+                       self.graph.shape[0], self.max_m, self.start)
+
+
+def load_nav(index_dir: str | Path, data_type: str) -> OracleNav | None:
+    """nav_index / nav_index.data / map.txt in the index directory or its nav/
+    child (bin/common/index_discovery.hpp:105-114); None when absent."""
+    index_dir = Path(index_dir)
+    nav_dir = next((d for d in (index_dir, index_dir / "nav") if (d / "nav_index").exists()), None)
+    if nav_dir is None:
+        return None
+    with open(nav_dir / "nav_index.data", "rb") as f:
+        n, data_len = struct.unpack("<ii", f.read(8))
+        data = np.fromfile(f, dtype=_DT[data_type][1], count=n * data_len).reshape(n, data_len)
+    mapping = np.array([int(x) for x in (nav_dir / "map.txt").read_text().split()[:n]], dtype=np.int32)
+    raw = np.fromfile(nav_dir / "nav_index", dtype="<i4")
+    max_m, start = int(raw[2]), int(raw[3])
+    graph = np.full((n, max_m), -1, dtype=np.int32)
+    pos = 6
+    for i in range(n):
+        d = int(raw[pos])
+        if not 0 < d <= max_m:
+            raise ValueError(f"nav node {i}: degree {d}")
+        graph[i, :d] = raw[pos + 1:pos + 1 + d]
+        pos += 1 + d
+    return OracleNav(np.ascontiguousarray(data), graph, mapping, start, max_m)
+
+
+def nav_entry(ix: OracleIndex, nav: OracleNav, query: np.ndarray) -> int:
+    q = np.ascontiguousarray(query, dtype=np.float32)
+    r = int(lib().orc_nav_entry(C.byref(ix._c), C.byref(nav._c), q.ctypes.data))
+    if r < 0:
+        raise RuntimeError(f"nav entry search failed with {r}")
+    return r
+
+
 def build_lut(ix: OracleIndex, query: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
     q = np.ascontiguousarray(query, dtype=np.float32)
     lut = np.empty((ix.num_chunks, 256), dtype=np.float32)
@@ -178,7 +234,7 @@ def exact_l2(ix: OracleIndex, q2: np.ndarray, v: int) -> float:
 
 def search(ix: OracleIndex, queries: np.ndarray, *, topk: int = 10, ef_search: int = 30, pipe_width: int = 1,
            early_exit_policy: str = "none", gpruning_warmup_steps: int = 10, gpruning_patience: int = 8,
-           num_threads: int = 0) -> dict:
+           num_threads: int = 0, nav: OracleNav | None = None) -> dict:
     q = np.ascontiguousarray(queries, dtype=np.float32)
     nq = q.shape[0]
     ids = np.empty((nq, topk), dtype=np.int32)
@@ -188,8 +244,9 @@ def search(ix: OracleIndex, queries: np.ndarray, *, topk: int = 10, ef_search: i
     nbrs = np.empty(nq, dtype=np.int64)
     pol = {"none": 0, "gpruning": 2}[early_exit_policy]
     p = _Params(topk, ef_search, pipe_width, pol, gpruning_warmup_steps, gpruning_patience, num_threads)
-    rc = lib().orc_search(C.byref(ix._c), q.ctypes.data, nq, C.byref(p), ids.ctypes.data, dists.ctypes.data,
-                          found.ctypes.data, steps.ctypes.data, nbrs.ctypes.data)
+    rc = lib().orc_search_nav(C.byref(ix._c), C.byref(nav._c) if nav is not None else None, q.ctypes.data, nq,
+                              C.byref(p), ids.ctypes.data, dists.ctypes.data, found.ctypes.data,
+                              steps.ctypes.data, nbrs.ctypes.data)
     if rc != 0:
         raise RuntimeError(f"oracle search failed with {rc}")
     return {"ids": ids, "dists": dists, "found": found, "steps": steps, "nbrs": nbrs}

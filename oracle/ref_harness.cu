@@ -52,7 +52,9 @@ extern "C" int ref_run_search(
     int64_t max_m, int64_t num_points, int64_t medoid, int32_t dtype, const uint8_t* codes, int32_t M,
     const float* pivots_t, const float* centroid, const int32_t* chunk_offsets, const float* queries, int32_t nq,
     int32_t topk, int32_t ef, int32_t early_policy, int32_t warmup, int32_t patience, int32_t num_blocks,
-    int32_t* out_ids, float* out_dists, int32_t* out_found, int32_t* out_steps, double timeout_s) {
+    int32_t* out_ids, float* out_dists, int32_t* out_found, int32_t* out_steps, double timeout_s,
+    const void* nav_data, const int32_t* nav_graph, const int32_t* nav_mapping, int32_t nav_num_node,
+    int32_t nav_max_m, int32_t nav_start) {
   using namespace quiver;
   int rc = 0;
   g_kernel_stuck = false;
@@ -63,7 +65,7 @@ extern "C" int ref_run_search(
     for (int i = chunk_offsets[c]; i < chunk_offsets[c + 1]; ++i) chunk_id[i] = c;
 
   DevBuf d_centroid, d_pivots_t, d_chunk_id, d_codes, d_pq_dists, d_pqdata, d_qdata, d_nid, d_ndist, d_ctx,
-      d_nns, d_dist, d_fc, d_next, d_done, d_finish, d_stop;
+      d_nns, d_dist, d_fc, d_next, d_done, d_finish, d_stop, d_nav_data, d_nav_graph, d_nav_map;
   IOControl* h_ctl = nullptr;
   uint8_t* h_buf = nullptr;
   PersistentKernelComm* h_comm = nullptr;
@@ -98,6 +100,17 @@ extern "C" int ref_run_search(
   HCK(cudaMalloc(&d_pqdata.p, sizeof(pqd)));
   HCK(cudaMemcpy(d_pqdata.p, &pqd, sizeof(pqd), cudaMemcpyHostToDevice));
 
+  // nav graph (NavGraph::init, nav_graph.cu:12-73: vectors, -1 padded rows, map)
+  if (nav_num_node > 0) {
+    const size_t vb = static_cast<size_t>(nav_num_node) * dim * (dtype == 1 ? 4 : 1);
+    HCK(cudaMalloc(&d_nav_data.p, vb));
+    HCK(cudaMemcpy(d_nav_data.p, nav_data, vb, cudaMemcpyHostToDevice));
+    HCK(cudaMalloc(&d_nav_graph.p, static_cast<size_t>(nav_num_node) * nav_max_m * 4));
+    HCK(cudaMemcpy(d_nav_graph.p, nav_graph, static_cast<size_t>(nav_num_node) * nav_max_m * 4,
+                   cudaMemcpyHostToDevice));
+    HCK(cudaMalloc(&d_nav_map.p, static_cast<size_t>(nav_num_node) * 4));
+    HCK(cudaMemcpy(d_nav_map.p, nav_mapping, static_cast<size_t>(nav_num_node) * 4, cudaMemcpyHostToDevice));
+  }
   HCK(cudaMalloc(&d_qdata.p, static_cast<size_t>(nq) * dim * 4));
   HCK(cudaMemcpy(d_qdata.p, queries, static_cast<size_t>(nq) * dim * 4, cudaMemcpyHostToDevice));
   HCK(cudaMalloc(&d_nid.p, static_cast<size_t>(num_blocks) * aligned_ef * 4));
@@ -154,6 +167,16 @@ extern "C" int ref_run_search(
   args.d_entry_nodes = nullptr;
   args.enter_point = static_cast<int32_t>(medoid);
   args.nav_data_dev = nullptr;
+  if (nav_num_node > 0) {  // what run_persistent_search sets (search.cu:597-605)
+    args.nav_data_dev = static_cast<uint8_t*>(d_nav_data.p);
+    args.nav_graph_dev = static_cast<int*>(d_nav_graph.p);
+    args.nav_mapping_dev = static_cast<int*>(d_nav_map.p);
+    args.nav_num_node = nav_num_node;
+    args.nav_data_len = static_cast<int>(dim);
+    args.nav_max_m = nav_max_m;
+    args.nav_start = nav_start;
+    args.nav_init_ef = ef < 5 ? ef : 5;
+  }
   args.pq_data = static_cast<shared::PQSearchData*>(d_pqdata.p);
   args.num_chunks = M;
   args.pq_dists = static_cast<float*>(d_pq_dists.p);

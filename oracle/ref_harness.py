@@ -46,8 +46,9 @@ def available() -> bool:
 
 def run(ix, queries: np.ndarray, *, topk: int = 10, ef_search: int = 30, early_exit_policy: str = "none",
         gpruning_warmup_steps: int = 10, gpruning_patience: int = 8, num_blocks: int = 64,
-        timeout_s: float = 60.0) -> dict:
-    """Search with the reference kernel at pipe width 1 on an oracle.OracleIndex."""
+        timeout_s: float = 60.0, nav=None) -> dict:
+    """Search with the reference kernel at pipe width 1 on an oracle.OracleIndex
+    (with its in-kernel nav entry search when `nav`, an oracle.OracleNav, is given)."""
     lib = C.CDLL(str(LIB))
     lib.ref_run_search.restype = C.c_int
     q = np.ascontiguousarray(queries, dtype=np.float32)
@@ -66,7 +67,12 @@ def run(ix, queries: np.ndarray, *, topk: int = 10, ef_search: int = 30, early_e
         C.c_void_p(ix.centroid.ctypes.data), C.c_void_p(ix.chunk_offsets.ctypes.data), C.c_void_p(q.ctypes.data),
         i32(nq), i32(topk), i32(ef_search), i32(pol), i32(gpruning_warmup_steps), i32(gpruning_patience),
         i32(num_blocks), C.c_void_p(ids.ctypes.data), C.c_void_p(dists.ctypes.data), C.c_void_p(found.ctypes.data),
-        C.c_void_p(steps.ctypes.data), C.c_double(timeout_s))
+        C.c_void_p(steps.ctypes.data), C.c_double(timeout_s),
+        C.c_void_p(nav.data.ctypes.data if nav is not None else None),
+        C.c_void_p(nav.graph.ctypes.data if nav is not None else None),
+        C.c_void_p(nav.mapping.ctypes.data if nav is not None else None),
+        i32(nav.graph.shape[0] if nav is not None else 0), i32(nav.max_m if nav is not None else 0),
+        i32(nav.start if nav is not None else 0))
     if rc != 0:
         raise RuntimeError(f"reference harness returned {rc}")
     return {"ids": ids, "dists": dists, "found": found, "steps": steps}

@@ -321,6 +321,15 @@ int main(int argc, char** argv) {
   }
   qv_index_info info{};
   qv_engine_info(eng, &info);
+  {
+    int32_t nav_nodes = 0, nav_m = 0, nav_start = 0;
+    qv_engine_nav_info(eng, &nav_nodes, &nav_m, &nav_start);
+    if (nav_nodes > 0)
+      std::cout << "[Quiver] NavGraph loaded: " << nav_nodes << " nodes, max_m=" << nav_m << ", start=" << nav_start
+                << std::endl;
+    else
+      std::cout << "[Quiver] No nav_index found in " << a.index_dir << ", skipping NavGraph" << std::endl;
+  }
 
   size_t dims = 0, nq = 0;
   std::vector<float> queries = load_queries_as_float(a.query_file, a.repeat, dims, nq);
@@ -349,6 +358,7 @@ int main(int argc, char** argv) {
     so.queries_per_block = a.queries_per_block;
     so.num_blocks = nb;
     so.early_exit_policy = policy;
+    so.skip_nav = a.skip_nav ? 1 : 0;
     qv_search_stats st{};
     const auto t0 = std::chrono::steady_clock::now();
     if (qv_search_timed(eng, queries.data(), static_cast<int64_t>(nq), info.dim, &so, ids.data(), dists.data(),

@@ -86,12 +86,18 @@ struct qv_engine {
   int64_t* d_nbrs = nullptr;
   int64_t* d_time = nullptr;
   int64_t cap_q = 0, cap_r = 0, cap_n = 0;
+  // nav graph (entry search); nav_num_node == 0: none
+  uint8_t* d_nav_data = nullptr;
+  int32_t* d_nav_graph = nullptr;
+  int32_t* d_nav_map = nullptr;
+  int32_t nav_num_node = 0, nav_max_m = 0, nav_start = 0;
 
   ~qv_engine() {
     if (device >= 0) cudaSetDevice(device);
     for (auto* p : {(void*)d_codes, (void*)d_pivots_t, (void*)d_centroid, (void*)d_chunk_off,
                     (void*)d_scratch, (void*)d_q, (void*)d_ids, (void*)d_dists, (void*)d_found,
-                    (void*)d_steps, (void*)d_nbrs, (void*)d_time})
+                    (void*)d_steps, (void*)d_nbrs, (void*)d_time, (void*)d_nav_data, (void*)d_nav_graph,
+                    (void*)d_nav_map})
       if (p) cudaFree(p);
     if (pages_host) {
       if (h_pages) cudaFreeHost(h_pages);
@@ -121,6 +127,7 @@ void validate_opts(const qv_engine* e, const qv_search_opts& o) {
   if (o.early_exit_policy != QV_EXIT_NONE && o.early_exit_policy != QV_EXIT_GPRUNING)
     fail(QV_ERR_INVALID_ARG, "early-exit policy must be none or gpruning");
   if (o.lut_mode != QV_LUT_FP32) fail(QV_ERR_UNSUPPORTED, "only the fp32 LUT mode is built");
+  if (o.skip_nav != 0 && o.skip_nav != 1) fail(QV_ERR_INVALID_ARG, "skip_nav must be 0 or 1");
   (void)e;
 }
 
@@ -245,6 +252,14 @@ qvk::SearchParams make_params(const qv_engine* e, const Plan& pl, const qv_searc
   p.gp_warmup = o.gpruning_warmup_steps;
   p.gp_patience = o.gpruning_patience;
   p.medoid = static_cast<int32_t>(e->L.medoid);
+  if (e->nav_num_node > 0 && !o.skip_nav) {
+    p.nav_data = e->d_nav_data;
+    p.nav_graph = e->d_nav_graph;
+    p.nav_mapping = e->d_nav_map;
+    p.nav_num_node = e->nav_num_node;
+    p.nav_max_m = e->nav_max_m;
+    p.nav_start = e->nav_start;
+  }
   p.lay = pl.lay;
   return p;
 }
@@ -262,6 +277,7 @@ void read_device_status(qv_engine* e) {
   const char* what = info[0] == qvk::kErrNeighborRange ? "a neighbour id >= num_points"
                    : info[0] == qvk::kErrDegree        ? "a stored degree above R"
                    : info[0] == qvk::kErrHopCap        ? "a walk beyond its iteration bound"
+                   : info[0] == qvk::kErrNav           ? "a nav graph id out of range or a nav walk beyond its bound"
                                                        : "an unknown device error";
   fail(QV_ERR_DEVICE, std::string("search kernel found ") + what + " (query " +
                           std::to_string(info[1]) + ", node/step " + std::to_string(info[2]) + ")");
@@ -299,6 +315,26 @@ void upload_pq(qv_engine* e, const float* pivots, const float* centroid, const i
   // +16 so 16-byte code loads of the last point stay inside the allocation
   CK(cudaMalloc(&e->d_codes, cb + 16));
   CK(cudaMemcpy(e->d_codes, codes, cb, cudaMemcpyHostToDevice));
+}
+
+// NavGraph::init's device copies (nav_graph.cu:70-72); replaces any earlier graph.
+void upload_nav(qv_engine* e, const qv::NavHost& nav) {
+  qv::check_nav(nav, e->L.dim, e->L.num_points);
+  for (void* p : {(void*)e->d_nav_data, (void*)e->d_nav_graph, (void*)e->d_nav_map})
+    if (p) CK(cudaFree(p));
+  e->d_nav_data = nullptr;
+  e->d_nav_graph = nullptr;
+  e->d_nav_map = nullptr;
+  e->nav_num_node = 0;
+  CK(cudaMalloc(&e->d_nav_data, nav.data.size()));
+  CK(cudaMemcpy(e->d_nav_data, nav.data.data(), nav.data.size(), cudaMemcpyHostToDevice));
+  CK(cudaMalloc(&e->d_nav_graph, nav.graph.size() * 4));
+  CK(cudaMemcpy(e->d_nav_graph, nav.graph.data(), nav.graph.size() * 4, cudaMemcpyHostToDevice));
+  CK(cudaMalloc(&e->d_nav_map, nav.mapping.size() * 4));
+  CK(cudaMemcpy(e->d_nav_map, nav.mapping.data(), nav.mapping.size() * 4, cudaMemcpyHostToDevice));
+  e->nav_num_node = nav.num_node;
+  e->nav_max_m = nav.max_m;
+  e->nav_start = nav.start;
 }
 
 void alloc_pages(qv_engine* e, int32_t page_store) {
@@ -400,6 +436,7 @@ void qv_search_opts_default(qv_search_opts* o) {
   o->early_exit_policy = QV_EXIT_GPRUNING;
   o->gpruning_warmup_steps = 10;
   o->gpruning_patience = 8;
+  o->skip_nav = 0;
   o->lut_mode = QV_LUT_FP32;
 }
 
@@ -464,6 +501,9 @@ int qv_engine_create(const qv_engine_opts* opts, qv_engine** out) {
       CK(cudaMemcpy(e->d_pages, host.data(), bytes, cudaMemcpyHostToDevice));
     }
     upload_pq(e.get(), pq.pivots.data(), pq.centroid.data(), pq.chunk_offsets.data(), pq.codes.data());
+    // search_setup.hpp:96-105: a nav graph next to the index is used when present
+    const std::string nav_dir = qv::find_nav_dir(dir);
+    if (!nav_dir.empty()) upload_nav(e.get(), qv::read_nav(nav_dir, qv::element_size(e->L.data_type)));
     *out = e.release();
   });
 }
@@ -504,6 +544,44 @@ int qv_engine_create_from_arrays(const qv_index_arrays* a, int32_t device, int32
       CK(cudaMemcpy(e->d_pages, a->pages, bytes, cudaMemcpyHostToDevice));
     upload_pq(e.get(), a->pivots, a->centroid, a->chunk_offsets, a->codes);
     *out = e.release();
+  });
+}
+
+int qv_engine_set_nav(qv_engine* e, const void* data, const int32_t* graph, const int32_t* mapping,
+                      int32_t num_node, int32_t max_m, int32_t start) {
+  return guarded([&] {
+    if (!e) fail(QV_ERR_INVALID_ARG, "null argument");
+    CK(cudaSetDevice(e->device));
+    if (num_node == 0) {
+      for (void* p : {(void*)e->d_nav_data, (void*)e->d_nav_graph, (void*)e->d_nav_map})
+        if (p) CK(cudaFree(p));
+      e->d_nav_data = nullptr;
+      e->d_nav_graph = nullptr;
+      e->d_nav_map = nullptr;
+      e->nav_num_node = 0;
+      return;
+    }
+    if (!data || !graph || !mapping) fail(QV_ERR_INVALID_ARG, "null argument");
+    if (num_node < 0 || max_m <= 0 || max_m > 32) fail(QV_ERR_INVALID_ARG, "num_node >= 0 and 0 < max_m <= 32");
+    qv::NavHost nav;
+    nav.num_node = num_node;
+    nav.data_len = static_cast<int32_t>(e->L.dim);
+    nav.max_m = max_m;
+    nav.start = start;
+    const size_t vb = static_cast<size_t>(num_node) * e->L.dim * qv::element_size(e->L.data_type);
+    nav.data.assign(static_cast<const uint8_t*>(data), static_cast<const uint8_t*>(data) + vb);
+    nav.graph.assign(graph, graph + static_cast<size_t>(num_node) * max_m);
+    nav.mapping.assign(mapping, mapping + num_node);
+    upload_nav(e, nav);
+  });
+}
+
+int qv_engine_nav_info(const qv_engine* e, int32_t* num_node, int32_t* max_m, int32_t* start) {
+  return guarded([&] {
+    if (!e || !num_node || !max_m || !start) fail(QV_ERR_INVALID_ARG, "null argument");
+    *num_node = e->nav_num_node;
+    *max_m = e->nav_max_m;
+    *start = e->nav_start;
   });
 }
 

@@ -224,4 +224,73 @@ int64_t validate_adjacency(const Layout& L, const uint8_t* pages) {
   return -1;
 }
 
+// nav_graph.cu:12-73: nav_index.data = i32 num_node, i32 data_len, vectors;
+// map.txt = num_node integers; nav_index = six i32 (field 2 max_m, field 3
+// start) then per node i32 degree and that many ids.
+NavHost read_nav(const std::string& nav_dir, int64_t elem_size) {
+  NavHost nav;
+  const std::string data_file = (fs::path(nav_dir) / "nav_index.data").string();
+  const std::string map_file = (fs::path(nav_dir) / "map.txt").string();
+  const std::string index_file = (fs::path(nav_dir) / "nav_index").string();
+  {
+    File f(data_file);
+    int32_t hdr[2];
+    f.read(hdr, sizeof(hdr), data_file);
+    nav.num_node = hdr[0];
+    nav.data_len = hdr[1];
+    if (nav.num_node <= 0 || nav.data_len <= 0)
+      throw IoError(QV_ERR_BAD_INDEX, "nav data header: num_node and data_len must be positive");
+    nav.data.resize(static_cast<size_t>(nav.num_node) * nav.data_len * elem_size);
+    f.read(nav.data.data(), nav.data.size(), data_file);
+  }
+  {
+    std::FILE* f = std::fopen(map_file.c_str(), "r");
+    if (!f) throw IoError(QV_ERR_IO, "Failed to open map file: " + map_file);
+    nav.mapping.resize(nav.num_node);
+    for (int32_t i = 0; i < nav.num_node; ++i) {
+      long x = -1;
+      if (std::fscanf(f, "%ld", &x) != 1) {
+        std::fclose(f);
+        throw IoError(QV_ERR_BAD_INDEX, "Failed to read map entry " + std::to_string(i) + " from " + map_file);
+      }
+      nav.mapping[i] = static_cast<int32_t>(x);
+    }
+    std::fclose(f);
+  }
+  {
+    File f(index_file);
+    int32_t hdr[6];
+    f.read(hdr, sizeof(hdr), index_file);
+    nav.max_m = hdr[2];
+    nav.start = hdr[3];
+    if (nav.max_m <= 0 || nav.max_m > 32)
+      throw IoError(QV_ERR_BAD_INDEX, "nav_index: max_m must be in (0, 32], got " + std::to_string(nav.max_m));
+    nav.graph.assign(static_cast<size_t>(nav.num_node) * nav.max_m, -1);
+    for (int32_t i = 0; i < nav.num_node; ++i) {
+      int32_t d = 0;
+      f.read(&d, 4, index_file);
+      if (d <= 0 || d > nav.max_m)
+        throw IoError(QV_ERR_BAD_INDEX, "nav_index: node " + std::to_string(i) + " has degree " +
+                                            std::to_string(d) + " outside (0, max_m]");
+      f.read(nav.graph.data() + static_cast<size_t>(i) * nav.max_m, 4 * static_cast<size_t>(d), index_file);
+    }
+  }
+  return nav;
+}
+
+void check_nav(const NavHost& nav, int64_t dim, int64_t num_points) {
+  if (nav.num_node <= 0) throw IoError(QV_ERR_BAD_INDEX, "nav graph has no nodes");
+  if (nav.max_m <= 0 || nav.max_m > 32) throw IoError(QV_ERR_BAD_INDEX, "nav max_m must be in (0, 32]");
+  if (nav.data_len != dim)
+    throw IoError(QV_ERR_BAD_INDEX, "nav vectors have " + std::to_string(nav.data_len) + " dims, the index " +
+                                        std::to_string(dim));
+  if (nav.start < 0 || nav.start >= nav.num_node) throw IoError(QV_ERR_BAD_INDEX, "nav start out of range");
+  for (size_t i = 0; i < nav.graph.size(); ++i)
+    if (nav.graph[i] < -1 || nav.graph[i] >= nav.num_node)
+      throw IoError(QV_ERR_BAD_INDEX, "nav graph id out of range at row " + std::to_string(i / nav.max_m));
+  for (int32_t i = 0; i < nav.num_node; ++i)
+    if (nav.mapping[i] < 0 || nav.mapping[i] >= num_points)
+      throw IoError(QV_ERR_BAD_INDEX, "nav map entry " + std::to_string(i) + " is not a base id");
+}
+
 }  // namespace qv

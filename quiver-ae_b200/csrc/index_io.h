@@ -7,6 +7,7 @@
 //   *_pq_compressed.bin       src/shared/index/pq_search.cu:67-68
 //   page file (header page skipped)  src/shared/io/mem_loader.cpp:28-85
 //   index discovery           bin/common/index_discovery.hpp:57-115
+//   nav graph                 src/shared/index/nav_graph.cu:12-73
 //   query / ground-truth bins bin/common/data_io.hpp:23-133
 // Errors are reported as qv::IoError (caught at the C ABI).
 #pragma once
@@ -60,5 +61,22 @@ void read_pages(const std::string& path, int64_t num_pages, const std::string& b
 // Scan every record: degree <= R and neighbour ids < N.  Returns the first
 // offending node or -1.
 int64_t validate_adjacency(const Layout& L, const uint8_t* pages);
+
+// A navigation graph as NavGraph::init reads it (nav_index, nav_index.data,
+// map.txt in one directory).  Rows of `graph` are max_m wide, -1 padded.
+struct NavHost {
+  int32_t num_node = 0, data_len = 0, max_m = 0, start = 0;
+  std::vector<uint8_t> data;      // [num_node x data_len] elements of the base type
+  std::vector<int32_t> graph;     // [num_node x max_m]
+  std::vector<int32_t> mapping;   // [num_node]
+};
+
+NavHost read_nav(const std::string& nav_dir, int64_t elem_size);
+
+// Checks the kernels rely on (the reference asserts some of them and reads
+// out of bounds on the rest): 0 < max_m <= 32, start < num_node, data_len ==
+// dim, graph ids -1 or < num_node, mapping ids < num_points.  Throws
+// IoError(QV_ERR_BAD_INDEX).
+void check_nav(const NavHost& nav, int64_t dim, int64_t num_points);
 
 }  // namespace qv

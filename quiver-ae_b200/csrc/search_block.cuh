@@ -70,6 +70,8 @@ enum : int {
   kMiscGHint = 66,  // hint after the merge
   kMiscDx = 67,     // [2] exact distance of each record's node (float bits)
   kMiscGRep = 72,   // [4] many-pair merge: sorted positions of pairs repeating an id
+  kMiscNavIdx = 76, // nav entry search: next slot to expand (-1: done)
+  kMiscNavErr = 77, // nav entry search: an id outside the nav graph
   kMiscSlots = 80,
 };
 
@@ -1001,6 +1003,56 @@ __device__ int expand_block(const SearchParams& p, const BSlot& s, uint32_t mask
   return 0;
 }
 
+// The nav entry search (see nav_select_warp) with the block's four warps
+// taking 7 neighbour slots each, as inkernel_nav.cuh:109-136 splits them;
+// warp 0 selects.  The queue lives in the many-pair sort buffer, free at
+// query start.  Returns the base id, or -1 after reporting kErrNav.
+template <typename T>
+__device__ int32_t nav_entry_block(const SearchParams& p, const BSlot& s, const float* q, int64_t qid) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  uint32_t* pid = s.sortbuf;
+  float* pd = reinterpret_cast<float*>(s.sortbuf + 32);
+  if (warp == 0) {
+    const float d0 = exact_l2_warp<T>(q, nav_vec<T>(p, p.nav_start), p.dim, lane);
+    pid[lane] = lane == 0 ? static_cast<uint32_t>(p.nav_start) : 0xffffffffu;
+    pd[lane] = lane == 0 ? d0 : __int_as_float(0x7f800000);
+  }
+  if (tid == 0) s.misc[kMiscNavErr] = 0;
+  __syncthreads();
+  const int64_t cap = 4 * static_cast<int64_t>(p.nav_num_node) + 64;
+  int idx = 0;
+  for (int64_t hop = 0; idx != -1; ++hop) {
+    const int32_t u = static_cast<int32_t>(pid[idx] & kIdMask);
+    if (hop > cap || u >= p.nav_num_node) {  // uniform: every thread read the same slot
+      report_error(p, kErrNav, qid, u, tid);
+      return -1;
+    }
+    __syncthreads();
+    if (tid == 0) pid[idx] |= kVisited;
+    if (!nav_fill_warp<T>(p, q, u, 7 * warp, 7 * warp + 7, pid, pd, lane) && lane == 0)
+      s.misc[kMiscNavErr] = 1;
+    __syncthreads();
+    if (s.misc[kMiscNavErr]) {
+      report_error(p, kErrNav, qid, u, tid);
+      return -1;
+    }
+    if (warp == 0) {
+      const int x = nav_select_warp(pid, pd, lane);
+      if (lane == 0) s.misc[kMiscNavIdx] = x;
+    }
+    __syncthreads();
+    idx = s.misc[kMiscNavIdx];
+  }
+  const uint32_t raw = pid[0] & kIdMask;
+  const int32_t entry = raw < static_cast<uint32_t>(p.nav_num_node) ? __ldg(p.nav_mapping + raw) : -1;
+  __syncthreads();  // everyone has read the queue before the sort buffer is reused
+  if (entry < 0 || entry >= p.num_points) {
+    report_error(p, kErrNav, qid, raw, tid);
+    return -1;
+  }
+  return entry;
+}
+
 template <typename T, int MC, int RP>
 __device__ void run_query_block(const SearchParams& p, const BSlot& s, int64_t qid) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -1010,12 +1062,14 @@ __device__ void run_query_block(const SearchParams& p, const BSlot& s, int64_t q
     s.rid[i] = -1;
     s.rdist[i] = __int_as_float(0x7f800000);
   }
-  if (tid < kMaxPipeWidth) s.lane[tid] = (tid == 0) ? p.medoid : -1;
+  int32_t entry = p.medoid;
+  if (p.nav_graph) entry = nav_entry_block<T>(p, s, p.queries + qid * p.dim, qid);
+  if (tid < kMaxPipeWidth) s.lane[tid] = (tid == 0) ? entry : -1;
   if (tid < kMiscWords && tid != kMiscQid) s.misc[tid] = 0;
   if (tid == kMiscLastTop1 || tid == kMiscLastTopk) s.misc[tid] = 0x7f800000;  // +inf
   __syncthreads();
 
-  int err = expand_block<T, MC, RP>(p, s, 1u, qid);  // boot: the entry on lane 0
+  int err = entry < 0 ? static_cast<int>(kErrNav) : expand_block<T, MC, RP>(p, s, 1u, qid);  // boot: lane 0
   if (!err) {
     // lanes 1..W-1 are seeded whether or not the boot hop stopped the query
     // (kernel_q1.cuh:367-371); their picks matter only when it did not

@@ -38,6 +38,7 @@ enum DeviceError : int32_t {
   kErrNeighborRange = 1,  // adjacency entry >= num_points
   kErrDegree = 2,         // stored degree > R
   kErrHopCap = 3,         // walk exceeded its iteration bound
+  kErrNav = 4,            // nav graph: id out of range or entry search over its bound
 };
 
 // Byte offsets of one query slot's arrays inside the CTA's shared memory.
@@ -84,6 +85,11 @@ struct SearchParams {
   int32_t ef, k, W;
   int32_t early_policy, gp_warmup, gp_patience;
   int32_t medoid;
+  // nav graph (entry search per query); nav_graph == nullptr: entry = medoid
+  const uint8_t* nav_data;       // [nav_num_node x dim], base data type
+  const int32_t* nav_graph;      // [nav_num_node x nav_max_m], -1 padded
+  const int32_t* nav_mapping;    // [nav_num_node] nav id -> base id
+  int32_t nav_num_node, nav_max_m, nav_start;
   SlotLayout lay;
 };
 
@@ -378,6 +384,131 @@ __device__ __forceinline__ void report_error(const SearchParams& p, int code, in
   }
 }
 
+
+// ---------------------------------------------------------------- nav entry
+// The entry search of src/quiver/kernel_core/inkernel_nav.cuh:60-201: a
+// 32-slot queue (4 best + 28 neighbours of the node expanded last), exact L2
+// (square_sum_32 order) on the query as given, before the centroid round
+// trip.  Results depend on its exact steps, restated here in this
+// repository's code:
+//   * neighbour i < 28 of node u is graph[max_m * u + i] (a row shorter than
+//     28 runs on into the next one; past the array's end it ends);
+//   * four chunks of 7 neighbour slots each stop at their first -1 and leave
+//     the rest of their slots as they were;
+//   * round i of four: a copy of the previous round's pick hands it its
+//     visited bit and drops out (the reference ORs from several lanes in one
+//     store; here every copy's bit is kept), then a shfl_down argmin tree
+//     (a value replaces only a strictly smaller one) names the slot moved to
+//     i, and the swap is skipped when the two distances are equal;
+//   * the walk goes on while one of the first four slots is unvisited.
+constexpr int kNavL = 4;
+constexpr int kNavR = 28;
+
+__device__ __forceinline__ int32_t nav_edge(const SearchParams& p, int32_t u, int i) {
+  const int64_t at = static_cast<int64_t>(p.nav_max_m) * u + i;
+  return at < static_cast<int64_t>(p.nav_num_node) * p.nav_max_m ? __ldg(p.nav_graph + at) : -1;
+}
+
+template <typename T>
+__device__ __forceinline__ const T* nav_vec(const SearchParams& p, int32_t v) {
+  return reinterpret_cast<const T*>(p.nav_data) + static_cast<int64_t>(v) * p.dim;
+}
+
+// One warp: neighbour slots [i0, i1) of nav node u (stops at the first -1).
+// Returns false on an id outside the nav graph.
+template <typename T>
+__device__ __forceinline__ bool nav_fill_warp(const SearchParams& p, const float* q, int32_t u, int i0, int i1,
+                                              uint32_t* pid, float* pd, int lane) {
+  for (int i = i0; i < i1; ++i) {
+    const int32_t v = nav_edge(p, u, i);
+    if (v == -1) break;
+    if (v < 0 || v >= p.nav_num_node) return false;
+    const float d = exact_l2_warp<T>(q, nav_vec<T>(p, v), p.dim, lane);
+    if (lane == 0) {
+      pid[i + kNavL] = static_cast<uint32_t>(v);
+      pd[i + kNavL] = d;
+    }
+  }
+  return true;
+}
+
+// One warp: the four selection rounds, then the first unvisited slot when it
+// is one of the first four (else -1), the same on every lane.
+__device__ __forceinline__ int nav_select_warp(uint32_t* pid, float* pd, int lane) {
+#pragma unroll 1
+  for (int i = 0; i < kNavL; ++i) {
+    float dist = pd[lane];
+    int pos = lane;
+    bool dup = false;
+    if (lane < i) dist = __int_as_float(0x7f800000);
+    else if (i != 0 && ((pid[lane] ^ pid[i - 1]) & kIdMask) == 0) dup = true;
+    __syncwarp();
+    if (dup) {
+      atomicOr(&pid[i - 1], pid[lane]);
+      pd[lane] = __int_as_float(0x7f800000);
+      dist = __int_as_float(0x7f800000);
+    }
+    __syncwarp();
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      const int op = __shfl_down_sync(kFull, pos, off);
+      const float od = __shfl_down_sync(kFull, dist, off);
+      if (od < dist) {
+        dist = od;
+        pos = op;
+      }
+    }
+    if (lane == 0 && i != pos) {
+      const float t = pd[i], y = pd[pos];
+      if (t != y) {
+        pd[i] = y;
+        pd[pos] = t;
+        const uint32_t m = pid[i];
+        pid[i] = pid[pos];
+        pid[pos] = m;
+      }
+    }
+    __syncwarp();
+  }
+  const unsigned unv = __ballot_sync(kFull, !(pid[lane] & kVisited));
+  const int x = unv ? __ffs(unv) - 1 : 32;
+  return x < kNavL ? x : -1;
+}
+
+// One warp, the whole entry search (the warp kernel).  Returns the base id,
+// or -1 after reporting kErrNav.
+template <typename T>
+__device__ int32_t nav_entry_warp(const SearchParams& p, const float* q, uint32_t* pid, float* pd, int64_t qid,
+                                  int lane) {
+  const float d0 = exact_l2_warp<T>(q, nav_vec<T>(p, p.nav_start), p.dim, lane);
+  pid[lane] = lane == 0 ? static_cast<uint32_t>(p.nav_start) : 0xffffffffu;
+  pd[lane] = lane == 0 ? d0 : __int_as_float(0x7f800000);
+  __syncwarp();
+  const int64_t cap = 4 * static_cast<int64_t>(p.nav_num_node) + 64;
+  int idx = 0;
+  for (int64_t hop = 0; idx != -1; ++hop) {
+    const int32_t u = static_cast<int32_t>(pid[idx] & kIdMask);
+    bool ok = hop <= cap && u < p.nav_num_node;
+    __syncwarp();
+    if (lane == 0) pid[idx] |= kVisited;
+    __syncwarp();
+    for (int w = 0; w < 4 && ok; ++w) ok = nav_fill_warp<T>(p, q, u, 7 * w, 7 * w + 7, pid, pd, lane);
+    if (!ok) {
+      report_error(p, kErrNav, qid, u, lane);
+      return -1;
+    }
+    __syncwarp();
+    idx = nav_select_warp(pid, pd, lane);
+  }
+  const uint32_t raw = pid[0] & kIdMask;
+  const int32_t entry = raw < static_cast<uint32_t>(p.nav_num_node) ? __ldg(p.nav_mapping + raw) : -1;
+  if (entry < 0 || entry >= p.num_points) {
+    report_error(p, kErrNav, qid, raw, lane);
+    return -1;
+  }
+  return entry;
+}
+
 __device__ __forceinline__ uint32_t code_byte(const uint4& v, int b) {
   const uint32_t w = (b < 4) ? v.x : (b < 8) ? v.y : (b < 12) ? v.z : v.w;
   return (w >> ((b & 3) * 8)) & 0xffu;
@@ -557,7 +688,12 @@ __device__ void run_query(const SearchParams& p, const Slot& s, int64_t qid, int
   }
   for (int w = lane; w < p.W; w += 32) s.lane[w] = -1;
   __syncwarp();
-  if (lane == 0) s.lane[0] = p.medoid;
+  int32_t entry = p.medoid;
+  if (p.nav_graph) {  // the neighbour arrays are free until the first merge
+    entry = nav_entry_warp<T>(p, p.queries + qid * p.dim, s.nid, s.ndist, qid, lane);
+    __syncwarp();
+  }
+  if (lane == 0) s.lane[0] = entry;
   __syncwarp();
 
   QueryState q;
@@ -572,7 +708,7 @@ __device__ void run_query(const SearchParams& p, const Slot& s, int64_t qid, int
   bool stop = false;
 
   // boot: expand the entry on lane 0, then seed lanes 1..W-1.
-  int err = expand_lanes<T, MC, SMAX>(p, s, q, 1u, stop, qid, lane);
+  int err = entry < 0 ? static_cast<int>(kErrNav) : expand_lanes<T, MC, SMAX>(p, s, q, 1u, stop, qid, lane);
   if (!err) {
     for (int w = 1; w < p.W; ++w) {
       const int32_t nx = select_warp(s, q.size, lane);

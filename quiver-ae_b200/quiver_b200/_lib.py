@@ -52,7 +52,7 @@ class SearchOpts(C.Structure):
         ("topk", C.c_int32), ("ef_search", C.c_int32), ("pipe_width", C.c_int32),
         ("queries_per_block", C.c_int32), ("num_blocks", C.c_int32),
         ("early_exit_policy", C.c_int32), ("gpruning_warmup_steps", C.c_int32),
-        ("gpruning_patience", C.c_int32), ("lut_mode", C.c_int32),
+        ("gpruning_patience", C.c_int32), ("lut_mode", C.c_int32), ("skip_nav", C.c_int32),
     ]
 
 
@@ -74,6 +74,10 @@ ENGINE_SYMBOLS = {
     "qv_engine_create": (C.c_int, [C.POINTER(EngineOpts), C.POINTER(C.c_void_p)]),
     "qv_engine_create_from_arrays": (C.c_int, [C.POINTER(IndexArrays), C.c_int32, C.c_int32, C.POINTER(C.c_void_p)]),
     "qv_engine_info": (C.c_int, [C.c_void_p, C.POINTER(IndexInfo)]),
+    "qv_engine_set_nav": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int32, C.c_int32,
+                                    C.c_int32]),
+    "qv_engine_nav_info": (C.c_int, [C.c_void_p, C.POINTER(C.c_int32), C.POINTER(C.c_int32),
+                                     C.POINTER(C.c_int32)]),
     "qv_engine_destroy": (None, [C.c_void_p]),
     "qv_search": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int64, C.c_int64, C.POINTER(SearchOpts),
                             C.c_void_p, C.c_void_p, C.c_void_p, C.POINTER(SearchStats)]),

@@ -114,3 +114,38 @@ def build_index(index_dir: str | Path, base: np.ndarray, *, R: int = 64, L: int 
     codes = pq_encode(base, pivots, centroid, offs, nthreads)
     formats.write_pq(index_dir / prefix, pivots, centroid, offs, codes)
     return BuiltIndex(index_dir, index_dir / prefix, data_type, layout)
+
+
+def nav_sample(n: int, n_nav: int, seed: int) -> np.ndarray:
+    """n_nav distinct base ids, ascending, chosen by a seeded permutation."""
+    rng = np.random.Generator(np.random.PCG64(seed + 0x6e6176))
+    return np.sort(rng.choice(n, size=min(n_nav, n), replace=False)).astype(np.int32)
+
+
+def build_nav(nav_dir: str | Path, base: np.ndarray, *, n_nav: int = 0, R: int = 28, L: int = 64,
+              alpha: float = 1.2, max_m: int = 32, seed: int = 0, nthreads: int = 0) -> formats.NavGraph:
+    """A navigation graph over a sample of the base set, in the reference's nav
+    format (src/shared/index/nav_graph.cu:12-73), for the in-kernel entry
+    search (src/quiver/kernel_core/inkernel_nav.cuh).
+
+    The reference repository has no producer of these files, so this one is
+    ours: a Vamana graph (degree R <= 28, the neighbours the entry search
+    reads per node) over n_nav seeded samples (default 1 % of the base, at
+    least 1,000), started at the sample's medoid, rows padded to max_m."""
+    base = np.ascontiguousarray(base)
+    n = base.shape[0]
+    if n_nav <= 0:
+        n_nav = max(1000, n // 100)
+    n_nav = min(n_nav, n)
+    if R > 28 or R > max_m:
+        raise ValueError("the entry search reads at most 28 neighbours per nav node")
+    ids = nav_sample(n, n_nav, seed)
+    sub = np.ascontiguousarray(base[ids])
+    graph, degree, medoid = vamana(sub, R, L, alpha, 2, seed, nthreads)
+    if np.any(degree <= 0):
+        raise ValueError("nav graph has a node without neighbours (sample too small)")
+    padded = np.full((len(ids), max_m), -1, dtype=np.int32)
+    padded[:, :R] = graph
+    nav = formats.NavGraph(sub, padded, degree.astype(np.int32), ids, int(medoid), max_m)
+    formats.write_nav(nav_dir, nav)
+    return nav

@@ -36,12 +36,13 @@ class SearchParams:
     gpruning_warmup_steps: int = 10
     gpruning_patience: int = 8
     lut_mode: int = _lib.QV_LUT_FP32
+    skip_nav: bool = False   # True: entry = medoid even when the engine holds a nav graph
 
     def to_c(self) -> _lib.SearchOpts:
         pol = {"none": _lib.QV_EXIT_NONE, "gpruning": _lib.QV_EXIT_GPRUNING}[self.early_exit_policy]
         return _lib.SearchOpts(self.topk, self.ef_search, self.pipe_width, self.queries_per_block,
                                self.num_blocks, pol, self.gpruning_warmup_steps, self.gpruning_patience,
-                               self.lut_mode)
+                               self.lut_mode, 1 if self.skip_nav else 0)
 
 
 class Engine:
@@ -97,6 +98,27 @@ class Engine:
 
     def __exit__(self, *exc):
         self.close()
+
+    def set_nav(self, data: np.ndarray | None, graph: np.ndarray | None = None, mapping: np.ndarray | None = None,
+                start: int = 0) -> None:
+        """Replace the nav graph (data [n x dim] of the index's type, graph [n x max_m] int32 -1 padded,
+        mapping [n] int32); data=None removes it."""
+        if data is None:
+            _check(self._lib.qv_engine_set_nav(self._h, None, None, None, 0, 0, 0))
+            return
+        data = np.ascontiguousarray(data)
+        graph = np.ascontiguousarray(graph, dtype=np.int32)
+        mapping = np.ascontiguousarray(mapping, dtype=np.int32)
+        _check(self._lib.qv_engine_set_nav(self._h, C.c_void_p(data.ctypes.data), C.c_void_p(graph.ctypes.data),
+                                           C.c_void_p(mapping.ctypes.data), graph.shape[0], graph.shape[1],
+                                           start))
+
+    @property
+    def nav_info(self) -> tuple[int, int, int]:
+        """(num_node, max_m, start); num_node 0 when the engine has no nav graph."""
+        n, m, st = C.c_int32(), C.c_int32(), C.c_int32()
+        _check(self._lib.qv_engine_nav_info(self._h, C.byref(n), C.byref(m), C.byref(st)))
+        return n.value, m.value, st.value
 
     @property
     def info(self) -> _lib.IndexInfo:

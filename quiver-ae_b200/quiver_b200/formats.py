@@ -14,6 +14,15 @@ Layouts (paths inside ruc-system/quiver-ae):
 * ``*_pq_compressed.bin`` -- [N x M] u8 codes.
 * ``.u8bin`` / ``.i8bin`` / ``.fbin`` / ``.ibin`` -- i32 n, i32 d, row-major data
   (bin/common/data_io.hpp:23-133).
+* nav graph directory (``<index>/nav_index`` or ``<index>/nav/nav_index``,
+  found as bin/common/index_discovery.hpp:105-114 does), read by
+  ``NavGraph::init`` (src/shared/index/nav_graph.cu:12-73):
+  ``nav_index`` -- six i32 (the loader uses field 2 = max_m <= 32 and field 3
+  = start; this writer puts num_node and data_len in fields 0 and 1, zeros in
+  4 and 5), then per node i32 degree d (0 < d <= max_m) and d i32 nav ids;
+  ``nav_index.data`` -- i32 num_node, i32 data_len, then num_node x data_len
+  vectors in the base data type; ``map.txt`` -- num_node whitespace-separated
+  base-graph ids (nav id -> base id).
 """
 from __future__ import annotations
 
@@ -165,3 +174,66 @@ def load_queries_as_float(path: str | Path, repeat: int = 1) -> np.ndarray:
     if repeat > 1:
         q = np.tile(q, (repeat, 1))
     return np.ascontiguousarray(q)
+
+
+@dataclass
+class NavGraph:
+    data: np.ndarray      # [num_node x dim], base data type
+    graph: np.ndarray     # [num_node x max_m] int32, -1 padded
+    degree: np.ndarray    # [num_node] int32
+    mapping: np.ndarray   # [num_node] int32, nav id -> base id
+    start: int
+    max_m: int
+
+
+def find_nav_dir(index_dir: str | Path) -> Path | None:
+    """The directory holding nav_index: the index directory or its nav/ child."""
+    index_dir = Path(index_dir)
+    for d in (index_dir, index_dir / "nav"):
+        if (d / "nav_index").exists():
+            return d
+    return None
+
+
+def write_nav(nav_dir: str | Path, nav: NavGraph) -> None:
+    nav_dir = Path(nav_dir)
+    nav_dir.mkdir(parents=True, exist_ok=True)
+    n, dim = nav.data.shape
+    if not 0 < nav.max_m <= 32:
+        raise ValueError("max_m must be in (0, 32]")
+    if np.any(nav.degree <= 0) or np.any(nav.degree > nav.max_m):
+        raise ValueError("every nav node needs 0 < degree <= max_m")
+    with open(nav_dir / "nav_index", "wb") as f:
+        f.write(struct.pack("<6i", n, dim, nav.max_m, nav.start, 0, 0))
+        for i in range(n):
+            d = int(nav.degree[i])
+            f.write(struct.pack("<i", d))
+            f.write(np.ascontiguousarray(nav.graph[i, :d], dtype=np.int32).tobytes())
+    with open(nav_dir / "nav_index.data", "wb") as f:
+        f.write(struct.pack("<ii", n, dim))
+        f.write(np.ascontiguousarray(nav.data).tobytes())
+    (nav_dir / "map.txt").write_text("\n".join(str(int(x)) for x in nav.mapping) + "\n")
+
+
+def read_nav(nav_dir: str | Path, data_type: str) -> NavGraph:
+    nav_dir = Path(nav_dir)
+    dt = NUMPY_DTYPES[data_type]
+    with open(nav_dir / "nav_index.data", "rb") as f:
+        n, dim = struct.unpack("<ii", f.read(8))
+        data = np.fromfile(f, dtype=dt, count=n * dim).reshape(n, dim)
+    mapping = np.array(( nav_dir / "map.txt").read_text().split()[:n], dtype=np.int32)
+    if mapping.size != n:
+        raise ValueError(f"map.txt holds {mapping.size} ids for {n} nav nodes")
+    raw = np.fromfile(nav_dir / "nav_index", dtype=np.int32)
+    max_m, start = int(raw[2]), int(raw[3])
+    graph = np.full((n, max_m), -1, dtype=np.int32)
+    degree = np.empty(n, dtype=np.int32)
+    pos = 6
+    for i in range(n):
+        d = int(raw[pos])
+        if not 0 < d <= max_m:
+            raise ValueError(f"nav node {i} has degree {d} outside (0, {max_m}]")
+        graph[i, :d] = raw[pos + 1:pos + 1 + d]
+        degree[i] = d
+        pos += 1 + d
+    return NavGraph(data, graph, degree, mapping, start, max_m)

@@ -10,6 +10,13 @@ Step 2 (a B200 box, reference harness built from the reference sources):
 own persistent kernel (oracle/_ref, pipe width 1) on both fixtures for every
 setting in SETTINGS and writes ``ref_<index>.npz`` into OUT_DIR; the files are
 then committed next to this script.
+
+Nav graphs: ``python tests/golden/make_ref_golden.py nav`` builds a nav
+graph for each fixture (quiver_b200.builder.build_nav, NAV_SIZES nodes) into
+``nav_<index>`` (kept apart from the index directory, which the engine and
+the reference would otherwise pick up); ``... refnav OUT_DIR`` runs the
+reference kernel with its in-kernel nav entry search on them for every
+setting in NAV_SETTINGS and writes ``ref_nav_<index>.npz``.
 """
 from __future__ import annotations
 
@@ -29,6 +36,39 @@ FIXTURES = {
 # (topk, ef_search, early_exit_policy)
 SETTINGS = [(10, 10, "none"), (10, 30, "none"), (10, 64, "none"), (10, 45, "gpruning"), (40, 50, "none"),
             (1, 16, "none")]
+
+
+NAV_SIZES = {"idx_u8": 200, "idx_f32": 120}
+NAV_SETTINGS = [(10, 10, "none"), (10, 30, "none"), (10, 64, "none"), (10, 45, "gpruning")]
+
+
+def nav_dir(name: str) -> Path:
+    return HERE / f"nav_{name.split('_', 1)[1]}"
+
+
+def make_navs() -> None:
+    from quiver_b200 import builder
+    for name, f in FIXTURES.items():
+        base = builder.synth_mixture(f["seed"], f["n"], f["dim"], f["centers"], f["sigma"], f["dtype"])
+        builder.build_nav(nav_dir(name), base, n_nav=NAV_SIZES[name], seed=f["seed"])
+
+
+def make_reference_nav_outputs(out_dir: Path) -> None:
+    from oracle import pyoracle, ref_harness
+    from quiver_b200 import formats
+    out_dir.mkdir(parents=True, exist_ok=True)
+    for name, f in FIXTURES.items():
+        ix = pyoracle.load_index(HERE / name, f["dtype"])
+        nav = pyoracle.load_nav(nav_dir(name), f["dtype"])
+        q = formats.read_bin(HERE / name / "queries.fbin", np.float32)
+        arrays = {}
+        for k, ef, pol in NAV_SETTINGS:
+            r = ref_harness.run(ix, q, topk=k, ef_search=ef, early_exit_policy=pol, nav=nav)
+            tag = f"k{k}_ef{ef}_{pol}"
+            for key, val in r.items():
+                arrays[f"{tag}_{key}"] = val
+        np.savez(out_dir / f"ref_nav_{name}.npz", **arrays)
+        print(f"wrote {out_dir / f'ref_nav_{name}.npz'}")
 
 
 def make_indexes() -> None:
@@ -62,5 +102,9 @@ def make_reference_outputs(out_dir: Path) -> None:
 if __name__ == "__main__":
     if sys.argv[1] == "index":
         make_indexes()
+    elif sys.argv[1] == "nav":
+        make_navs()
+    elif sys.argv[1] == "refnav":
+        make_reference_nav_outputs(Path(sys.argv[2]))
     else:
         make_reference_outputs(Path(sys.argv[2]))
