@@ -40,6 +40,10 @@ def log(*a):
     print(*a, file=sys.stderr, flush=True)
 
 
+def entry_desc(nav_nodes: int) -> str:
+    return f"nav graph entry search ({nav_nodes} nodes)" if nav_nodes else "medoid (no nav graph)"
+
+
 def workload_desc(w) -> str:
     return (f"{w.name}: {w.n // 1_000_000 if w.n >= 1_000_000 else w.n}{'M' if w.n >= 1_000_000 else ''} x {w.dim}-d "
             f"{w.data_type} seeded {w.centers}-cluster Gaussian mixture (sigma {w.sigma}); Vamana R={w.R} "
@@ -141,9 +145,10 @@ def reference_arm(args, rank: int, world: int) -> int:
     w = workloads.CONFIGS[args.config]
     d = workloads.prepare(w, log=log)
     ix = pyoracle.load_index(d, w.data_type)
+    nav = pyoracle.load_nav(workloads.prepare_nav(w, log=log), w.data_type) if args.nav else None
     qc = workloads.queries(w, rows=CALIB_QUERIES).astype(np.float32)
     gtc = workloads.ground_truth(w, qc, 10)
-    search_kw = dict(topk=w.topk, pipe_width=args.pipe_width, early_exit_policy=args.early_exit)
+    search_kw = dict(topk=w.topk, pipe_width=args.pipe_width, early_exit_policy=args.early_exit, nav=nav)
     if args.ef > 0:
         ef = args.ef
         recall = pyoracle.calc_recall(pyoracle.search(ix, qc, ef_search=ef, **search_kw)["ids"], gtc, 10)
@@ -172,7 +177,8 @@ def reference_arm(args, rank: int, world: int) -> int:
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded Gaussian mixture; SIFT/DEEP not present)",
         "config": {"workload": workload_desc(w), "ef_search": ef, "recall_at_10": recall,
-                   "pipe_width": args.pipe_width, "early_exit": args.early_exit},
+                   "pipe_width": args.pipe_width, "early_exit": args.early_exit,
+                   "entry": entry_desc(nav.graph.shape[0] if nav is not None else 0)},
         "cpu_baseline": {"value": qps, "unit": "queries/s", "cores": cores, "kind": "port", "sample": sample},
         "e2e": {"value": qps, "unit": "queries/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "recall_at_10": recall,
@@ -187,7 +193,8 @@ def cpu_baseline(w, d, ef: int, args) -> dict:
     from quiver_b200 import workloads
     ix = pyoracle.load_index(d, w.data_type)
     q = workloads.queries(w).astype(np.float32)
-    kw = dict(topk=w.topk, ef_search=ef, pipe_width=args.pipe_width, early_exit_policy=args.early_exit)
+    nav = pyoracle.load_nav(d / "nav", w.data_type) if args.nav else None
+    kw = dict(topk=w.topk, ef_search=ef, pipe_width=args.pipe_width, early_exit_policy=args.early_exit, nav=nav)
     t = time.perf_counter()
     pyoracle.search(ix, q[:256], **kw)
     rate = 256 / max(time.perf_counter() - t, 1e-6)
@@ -211,6 +218,8 @@ def main() -> int:
     ap.add_argument("--pipe-width", type=int, default=2)
     ap.add_argument("--early-exit", default="none", choices=["none", "gpruning"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--nav", action="store_true",
+                    help="start each query from the nav-graph entry search (a 1 %% nav graph is built and cached)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -243,9 +252,12 @@ def main() -> int:
     w = workloads.CONFIGS[args.config]
     if rank == 0:
         workloads.prepare(w, log=log)
+        if args.nav:
+            workloads.prepare_nav(w, log=log)
     barrier()
     d = workloads.index_dir(w)
     eng = Engine.open(d, w.data_type, device=local)
+    nav_nodes = eng.nav_info[0] if args.nav else 0
 
     # ef calibration on the first CALIB_QUERIES rows (identical on every rank)
     qc = workloads.queries(w, rows=CALIB_QUERIES)
@@ -256,7 +268,8 @@ def main() -> int:
     from quiver_b200.recall import calc_recall
 
     def params(ef):
-        return SearchParams(topk=w.topk, ef_search=ef, pipe_width=args.pipe_width, early_exit_policy=args.early_exit)
+        return SearchParams(topk=w.topk, ef_search=ef, pipe_width=args.pipe_width, early_exit_policy=args.early_exit,
+                            skip_nav=not args.nav)
 
     def recall_of(ef):
         return calc_recall(eng.search(qc, params(ef))[0], gtc, 10)
@@ -335,6 +348,7 @@ def main() -> int:
             "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded Gaussian mixture; SIFT/DEEP not present)",
             "config": {"workload": workload_desc(w), "ef_search": ef, "recall_at_10": recall,
+                       "entry": entry_desc(nav_nodes),
                        "recall_at_10_step_batch": step_recall, "pipe_width": args.pipe_width,
                        "early_exit": args.early_exit, "queries_per_step_per_gpu": nq,
                        "l2": f"inputs larger than L2: page store {info.num_pages * 4096 / 1e6:.0f} MB + codes "

@@ -86,6 +86,22 @@ def prepare(w: Workload, log=print) -> Path:
     return d
 
 
+def prepare_nav(w: Workload, log=print) -> Path:
+    """Build (or reuse) a nav graph for the index of `w` in its nav/ child
+    (builder.build_nav defaults: a 1 % sample, degree 28)."""
+    d = prepare(w, log=log)
+    nav_dir = d / "nav"
+    stamp = nav_dir / "nav.json"
+    want = {"workload": asdict(w), "n_nav": 0, "seed": w.seed}
+    if stamp.exists() and json.loads(stamp.read_text()) == want:
+        return nav_dir
+    t0 = time.time()
+    nav = builder.build_nav(nav_dir, base(w), seed=w.seed)
+    log(f"[workload] {w.name}: nav graph of {nav.graph.shape[0]} nodes built in {time.time() - t0:.1f}s")
+    stamp.write_text(json.dumps(want))
+    return nav_dir
+
+
 def ground_truth(w: Workload, q: np.ndarray, k: int = 10, device: str | None = None) -> np.ndarray:
     """Exact top-k of `q` against the base set (GPU brute force when a device is given)."""
     d = index_dir(w)
