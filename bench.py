@@ -148,7 +148,8 @@ def reference_arm(args, rank: int, world: int) -> int:
     nav = pyoracle.load_nav(workloads.prepare_nav(w, log=log), w.data_type) if args.nav else None
     qc = workloads.queries(w, rows=CALIB_QUERIES).astype(np.float32)
     gtc = workloads.ground_truth(w, qc, 10)
-    search_kw = dict(topk=w.topk, pipe_width=args.pipe_width, early_exit_policy=args.early_exit, nav=nav)
+    search_kw = dict(topk=w.topk, pipe_width=args.pipe_width, early_exit_policy=args.early_exit, nav=nav,
+                     visited_filter=args.visited_filter)
     if args.ef > 0:
         ef = args.ef
         recall = pyoracle.calc_recall(pyoracle.search(ix, qc, ef_search=ef, **search_kw)["ids"], gtc, 10)
@@ -178,7 +179,8 @@ def reference_arm(args, rank: int, world: int) -> int:
         "data": "synthetic (seeded Gaussian mixture; SIFT/DEEP not present)",
         "config": {"workload": workload_desc(w), "ef_search": ef, "recall_at_10": recall,
                    "pipe_width": args.pipe_width, "early_exit": args.early_exit,
-                   "entry": entry_desc(nav.graph.shape[0] if nav is not None else 0)},
+                   "entry": entry_desc(nav.graph.shape[0] if nav is not None else 0),
+                   "visited_filter": args.visited_filter},
         "cpu_baseline": {"value": qps, "unit": "queries/s", "cores": cores, "kind": "port", "sample": sample},
         "e2e": {"value": qps, "unit": "queries/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "recall_at_10": recall,
@@ -194,7 +196,8 @@ def cpu_baseline(w, d, ef: int, args) -> dict:
     ix = pyoracle.load_index(d, w.data_type)
     q = workloads.queries(w).astype(np.float32)
     nav = pyoracle.load_nav(d / "nav", w.data_type) if args.nav else None
-    kw = dict(topk=w.topk, ef_search=ef, pipe_width=args.pipe_width, early_exit_policy=args.early_exit, nav=nav)
+    kw = dict(topk=w.topk, ef_search=ef, pipe_width=args.pipe_width, early_exit_policy=args.early_exit, nav=nav,
+              visited_filter=args.visited_filter)
     t = time.perf_counter()
     pyoracle.search(ix, q[:256], **kw)
     rate = 256 / max(time.perf_counter() - t, 1e-6)
@@ -218,6 +221,10 @@ def main() -> int:
     ap.add_argument("--pipe-width", type=int, default=2)
     ap.add_argument("--early-exit", default="none", choices=["none", "gpruning"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--latency", default="",
+                    help="also time small batches end to end, e.g. 1,4,16 (latency mode; rank 0 only)")
+    ap.add_argument("--visited-filter", action="store_true",
+                    help="the engine's visited-filter mode (not reference behaviour; reports its recall)")
     ap.add_argument("--nav", action="store_true",
                     help="start each query from the nav-graph entry search (a 1 %% nav graph is built and cached)")
     args = ap.parse_args()
@@ -269,7 +276,7 @@ def main() -> int:
 
     def params(ef):
         return SearchParams(topk=w.topk, ef_search=ef, pipe_width=args.pipe_width, early_exit_policy=args.early_exit,
-                            skip_nav=not args.nav)
+                            skip_nav=not args.nav, visited_filter=args.visited_filter)
 
     def recall_of(ef):
         return calc_recall(eng.search(qc, params(ef))[0], gtc, 10)
@@ -337,6 +344,22 @@ def main() -> int:
     step_recall = calc_recall(h_ids.numpy(), workloads.ground_truth(w, q, 10, device=f"cuda:{local}"), 10) \
         if rank == 0 else None
 
+    # latency mode: batches of a few queries through qv_search (pinned host
+    # buffers in and out, one kernel per batch), wall time per batch
+    latency = {}
+    if args.latency and rank == 0:
+        for b in (int(x) for x in args.latency.split(",") if x):
+            reps = max(50, 1000 // b)
+            times = []
+            for r in range(reps + 5):
+                r0 = (r * b) % (nq - b + 1)
+                t1 = time.perf_counter()
+                eng.search_host_ptrs(hq[r0:].data_ptr(), b, info.dim, p, h_ids.data_ptr(), h_dists.data_ptr())
+                if r >= 5:
+                    times.append((time.perf_counter() - t1) * 1e3)
+            latency[str(b)] = {"batches": reps, "p50_ms": float(np.percentile(times, 50)),
+                               "p99_ms": float(np.percentile(times, 99)), "qps": b * 1e3 / statistics.mean(times)}
+
     if rank == 0:
         peaks = read_peaks()
         avg_ms = statistics.mean(step_ms)
@@ -348,7 +371,7 @@ def main() -> int:
             "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded Gaussian mixture; SIFT/DEEP not present)",
             "config": {"workload": workload_desc(w), "ef_search": ef, "recall_at_10": recall,
-                       "entry": entry_desc(nav_nodes),
+                       "entry": entry_desc(nav_nodes), "visited_filter": args.visited_filter,
                        "recall_at_10_step_batch": step_recall, "pipe_width": args.pipe_width,
                        "early_exit": args.early_exit, "queries_per_step_per_gpu": nq,
                        "l2": f"inputs larger than L2: page store {info.num_pages * 4096 / 1e6:.0f} MB + codes "
@@ -364,6 +387,10 @@ def main() -> int:
             "gpu_launches": args.steps,
             "clocks": clocks,
         }
+        if latency:
+            line["latency_mode"] = {"per_batch_size": latency,
+                                    "how": "qv_search on pinned host buffers, host wall time per batch "
+                                           "(H2D, one kernel, D2H, sync), same ef / pipe width"}
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(w, d, ef, args)
         print(json.dumps(line), flush=True)

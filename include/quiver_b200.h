@@ -112,6 +112,11 @@ typedef struct {
   int32_t skip_nav;               /* 1: start every query at the medoid even when the engine holds
                                      a nav graph (the CLI's --skip-nav, bin/quiver_search.cu:118-122,
                                      241-245); default 0 */
+  int32_t visited_filter;         /* 1: a node a query has scheduled for expansion never re-enters its
+                                     candidate list, so no node is expanded twice and the top-k holds
+                                     no repeats.  A mode of this engine, not reference behaviour (the
+                                     reference tracks visited nodes only inside the list); results then
+                                     differ from the reference's.  Needs one query per CTA; default 0 */
 } qv_search_opts;
 
 typedef struct {

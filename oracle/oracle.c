@@ -97,7 +97,37 @@ typedef struct {
   int32_t* rid; float* rdist; int fc;         /* top-k: nns / distances / found_cnt */
   float* lut; float* q2;
   int64_t nbrs;                               /* neighbours scored */
+  /* visited-filter mode: ids scheduled for expansion this query (open
+   * addressing, id + 1, 0 = empty) */
+  uint32_t* vset; int64_t vcap, vcount; int vfilter;
 } orc_ctx;
+
+static uint64_t vhash(uint32_t id) { return (uint64_t)id * 0x9E3779B97F4A7C15ull; }
+
+static int vset_has(const orc_ctx* c, uint32_t id) {
+  for (uint64_t h = vhash(id) & (c->vcap - 1);; h = (h + 1) & (c->vcap - 1)) {
+    if (c->vset[h] == 0) return 0;
+    if (c->vset[h] == id + 1) return 1;
+  }
+}
+
+static void vset_add(orc_ctx* c, uint32_t id) {
+  if (2 * (c->vcount + 1) > c->vcap) {  /* grow */
+    const int64_t old = c->vcap;
+    uint32_t* prev = c->vset;
+    c->vcap = old * 2;
+    c->vset = (uint32_t*)calloc((size_t)c->vcap, sizeof(uint32_t));
+    c->vcount = 0;
+    for (int64_t i = 0; i < old; ++i)
+      if (prev[i]) vset_add(c, prev[i] - 1);
+    free(prev);
+  }
+  uint64_t h = vhash(id) & (c->vcap - 1);
+  for (; c->vset[h] != 0; h = (h + 1) & (c->vcap - 1))
+    if (c->vset[h] == id + 1) return;
+  c->vset[h] = id + 1;
+  c->vcount++;
+}
 
 /* gpu_primitives.cuh:140-153: first index in [l, r) whose (dist, id&mask)
  * key is not below (d, x&mask). */
@@ -148,6 +178,16 @@ static int orc_merge(const orc_index* ix, orc_ctx* c, int64_t node, int ef) {
     c->tdist[sz + t] = orc_adc(c->lut, ix->codes + (int64_t)nb * M, M);
   }
   c->nbrs += deg;
+  if (c->vfilter) {  /* visited-filter mode: drop ids already scheduled for expansion */
+    uint32_t kept = 0;
+    for (uint32_t t = 0; t < deg; ++t) {
+      if (vset_has(c, c->tid[sz + t])) continue;
+      c->tid[sz + kept] = c->tid[sz + t];
+      c->tdist[sz + kept] = c->tdist[sz + t];
+      ++kept;
+    }
+    deg = kept;
+  }
   /* 300-329: sort the deg new pairs ascending by (dist, id&mask).  Keys are
    * distinct for an index whose adjacency lists hold distinct ids, so any
    * correct sort gives the reference's order.  Binary insertion sort. */
@@ -410,6 +450,12 @@ static int orc_search_one(const orc_index* ix, const orc_nav* nav, orc_ctx* c, c
     entry = orc_nav_entry(ix, nav, q);
     if (entry < 0) return (int)entry;
   }
+  c->vfilter = p->visited_filter;
+  if (c->vfilter) {
+    memset(c->vset, 0, sizeof(uint32_t) * c->vcap);
+    c->vcount = 0;
+    vset_add(c, (uint32_t)entry);
+  }
   int rc = orc_merge(ix, c, entry, ef);
   if (rc) return rc;
   lane_req[0] = orc_visit_select(ix, c, entry, ef, k);
@@ -426,6 +472,9 @@ static int orc_search_one(const orc_index* ix, const orc_nav* nav, orc_ctx* c, c
     for (int w = 0; w < W; ++w) { active[w] = lane_req[w] != -1; any |= active[w]; }
     if (!any) break;                              /* converged, 421-425 */
     if (++iters > max_iters) return -3;
+    if (c->vfilter)
+      for (int w = 0; w < W; ++w)
+        if (active[w]) vset_add(c, (uint32_t)lane_req[w]);
     for (int w = 0; w < W; ++w) {
       if (!active[w]) continue;
       const int64_t node = lane_req[w];
@@ -475,6 +524,8 @@ int orc_search_nav(const orc_index* ix, const orc_nav* nav, const float* queries
     c.rdist = (float*)malloc(sizeof(float) * p->topk);
     c.lut = (float*)malloc(sizeof(float) * (size_t)ix->num_chunks * ORC_PIVOTS);
     c.q2 = (float*)malloc(sizeof(float) * ix->dim);
+    c.vcap = 1024;
+    c.vset = (uint32_t*)calloc((size_t)c.vcap, sizeof(uint32_t));
     int32_t lane_req[64];
 #ifdef _OPENMP
 #pragma omp for schedule(dynamic, 8)
@@ -497,7 +548,7 @@ int orc_search_nav(const orc_index* ix, const orc_nav* nav, const float* queries
       if (nbrs) nbrs[qi] = c.nbrs;
     }
     free(c.lid); free(c.ldist); free(c.tid); free(c.tdist); free(c.mid);
-    free(c.mdist); free(c.mpos); free(c.rid); free(c.rdist); free(c.lut); free(c.q2);
+    free(c.mdist); free(c.mpos); free(c.rid); free(c.rdist); free(c.lut); free(c.q2); free(c.vset);
   }
   return err;
 }

@@ -62,6 +62,8 @@ typedef struct {
   int32_t gpruning_warmup_steps;
   int32_t gpruning_patience;
   int32_t num_threads;          /* OpenMP threads for orc_search; <=0 means all */
+  int32_t visited_filter;       /* 1: a node scheduled for expansion never re-enters the list
+                                   (a mode of this build, not reference behaviour); 0: reference */
 } orc_params;
 
 /* A navigation graph (src/shared/index/nav_graph.cu:12-73).  Vectors have

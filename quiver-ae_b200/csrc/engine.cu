@@ -91,13 +91,17 @@ struct qv_engine {
   int32_t* d_nav_graph = nullptr;
   int32_t* d_nav_map = nullptr;
   int32_t nav_num_node = 0, nav_max_m = 0, nav_start = 0;
+  // visited-filter mode: per-CTA tables, tags never reused until the counter wraps
+  unsigned long long* d_visited = nullptr;
+  size_t visited_bytes = 0;
+  uint32_t visited_next = 1;
 
   ~qv_engine() {
     if (device >= 0) cudaSetDevice(device);
     for (auto* p : {(void*)d_codes, (void*)d_pivots_t, (void*)d_centroid, (void*)d_chunk_off,
                     (void*)d_scratch, (void*)d_q, (void*)d_ids, (void*)d_dists, (void*)d_found,
                     (void*)d_steps, (void*)d_nbrs, (void*)d_time, (void*)d_nav_data, (void*)d_nav_graph,
-                    (void*)d_nav_map})
+                    (void*)d_nav_map, (void*)d_visited})
       if (p) cudaFree(p);
     if (pages_host) {
       if (h_pages) cudaFreeHost(h_pages);
@@ -128,6 +132,7 @@ void validate_opts(const qv_engine* e, const qv_search_opts& o) {
     fail(QV_ERR_INVALID_ARG, "early-exit policy must be none or gpruning");
   if (o.lut_mode != QV_LUT_FP32) fail(QV_ERR_UNSUPPORTED, "only the fp32 LUT mode is built");
   if (o.skip_nav != 0 && o.skip_nav != 1) fail(QV_ERR_INVALID_ARG, "skip_nav must be 0 or 1");
+  if (o.visited_filter != 0 && o.visited_filter != 1) fail(QV_ERR_INVALID_ARG, "visited_filter must be 0 or 1");
   (void)e;
 }
 
@@ -141,6 +146,8 @@ Plan make_plan(qv_engine* e, const qv_search_opts& o, int64_t nq) {
   // Q >= 2: Q one-warp query slots per CTA (the warp kernel).  Both give
   // identical results.
   pl.block = o.queries_per_block <= 1;
+  if (o.visited_filter && !pl.block)
+    fail(QV_ERR_UNSUPPORTED, "the visited-filter mode runs with one query per CTA (queries_per_block 0 or 1)");
   const int rp = 32 * pl.smax;
   const int G = pl.block ? qvk::kBlock / rp : (pl.smax <= 2 ? 4 : 2);
   int64_t off = 0;
@@ -264,6 +271,34 @@ qvk::SearchParams make_params(const qv_engine* e, const Plan& pl, const qv_searc
   return p;
 }
 
+// Visited-filter mode: one table of `cap` entries per persistent CTA; query
+// qid of this search gets tag visited_next + qid (tags start at 1, 0 means
+// empty), so tables are zeroed only when allocated or when the counter wraps.
+void prepare_visited(qv_engine* e, const Plan& pl, const qv_search_opts& o, int64_t nq, qvk::SearchParams& p,
+                     cudaStream_t st) {
+  if (!o.visited_filter) return;
+  int cap = 1024;
+  while (cap < 8 * o.ef_search) cap <<= 1;
+  const size_t need = static_cast<size_t>(pl.grid) * cap * sizeof(unsigned long long);
+  if (need > e->visited_bytes) {
+    if (e->d_visited) CK(cudaFree(e->d_visited));
+    e->d_visited = nullptr;
+    e->visited_bytes = 0;
+    CK(cudaMalloc(&e->d_visited, need));
+    e->visited_bytes = need;
+    CK(cudaMemsetAsync(e->d_visited, 0, need, st));
+    e->visited_next = 1;
+  }
+  if (static_cast<uint64_t>(e->visited_next) + static_cast<uint64_t>(nq) + 1 >= (1ull << 32)) {
+    CK(cudaMemsetAsync(e->d_visited, 0, e->visited_bytes, st));
+    e->visited_next = 1;
+  }
+  p.visited = e->d_visited;
+  p.visited_cap = cap;
+  p.visited_tag0 = e->visited_next;
+  e->visited_next += static_cast<uint32_t>(nq);
+}
+
 void enqueue_search(qv_engine* e, const Plan& pl, const qvk::SearchParams& p, cudaStream_t st) {
   CK(cudaMemsetAsync(e->d_scratch, 0, 8 * sizeof(int32_t), st));
   pl.launch(p, pl.grid, pl.threads, pl.smem, st);
@@ -278,6 +313,7 @@ void read_device_status(qv_engine* e) {
                    : info[0] == qvk::kErrDegree        ? "a stored degree above R"
                    : info[0] == qvk::kErrHopCap        ? "a walk beyond its iteration bound"
                    : info[0] == qvk::kErrNav           ? "a nav graph id out of range or a nav walk beyond its bound"
+                   : info[0] == qvk::kErrVisited       ? "a full visited-filter table"
                                                        : "an unknown device error";
   fail(QV_ERR_DEVICE, std::string("search kernel found ") + what + " (query " +
                           std::to_string(info[1]) + ", node/step " + std::to_string(info[2]) + ")");
@@ -437,6 +473,7 @@ void qv_search_opts_default(qv_search_opts* o) {
   o->gpruning_warmup_steps = 10;
   o->gpruning_patience = 8;
   o->skip_nav = 0;
+  o->visited_filter = 0;
   o->lut_mode = QV_LUT_FP32;
 }
 
@@ -635,9 +672,10 @@ static int search_host(qv_engine* e, const float* queries, int64_t nq, int64_t d
     CK(cudaEventRecord(e->ev[0], st));
     CK(cudaMemcpyAsync(e->d_q, queries, nq * dim * 4, cudaMemcpyHostToDevice, st));
     CK(cudaEventRecord(e->ev[1], st));
-    const auto p = make_params(e, pl, *opts, e->d_q, nq, e->d_ids, e->d_dists, e->d_found,
-                               want_counts ? e->d_steps : nullptr, want_counts ? e->d_nbrs : nullptr,
-                               query_ms ? e->d_time : nullptr);
+    auto p = make_params(e, pl, *opts, e->d_q, nq, e->d_ids, e->d_dists, e->d_found,
+                         want_counts ? e->d_steps : nullptr, want_counts ? e->d_nbrs : nullptr,
+                         query_ms ? e->d_time : nullptr);
+    prepare_visited(e, pl, *opts, nq, p, st);
     enqueue_search(e, pl, p, st);
     CK(cudaEventRecord(e->ev[2], st));
     CK(cudaMemcpyAsync(ids, e->d_ids, nq * opts->topk * 4, cudaMemcpyDeviceToHost, st));
@@ -693,7 +731,8 @@ int qv_search_device(qv_engine* e, const float* d_queries, int64_t nq, const qv_
     const Plan pl = make_plan(e, *opts, std::max<int64_t>(nq, 1));
     if (nq == 0) return;
     cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : e->stream;
-    const auto p = make_params(e, pl, *opts, d_queries, nq, d_ids, d_dists, d_found, d_steps, d_nbrs);
+    auto p = make_params(e, pl, *opts, d_queries, nq, d_ids, d_dists, d_found, d_steps, d_nbrs);
+    prepare_visited(e, pl, *opts, nq, p, st);
     enqueue_search(e, pl, p, st);
   });
 }
@@ -762,6 +801,8 @@ int qv_search_noalloc(qv_engine* e, const float* queries, int64_t nq, int64_t di
     if (dim != e->L.dim)
       fail(QV_ERR_INVALID_ARG, "Query dimension mismatch: queries have " + std::to_string(dim) +
                                    " dims, but the index expects " + std::to_string(e->L.dim));
+    if (opts->visited_filter)
+      fail(QV_ERR_UNSUPPORTED, "the visited-filter mode needs per-CTA device tables; use qv_search");
     CK(cudaSetDevice(e->device));
     const Plan pl = make_plan(e, *opts, std::max<int64_t>(nq, 1));
     if (nq == 0) return;

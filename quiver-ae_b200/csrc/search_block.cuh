@@ -312,6 +312,8 @@ __device__ __forceinline__ void merge_visit_select(const SearchParams& p, const 
     if (cand) {
       r = lower_bound_s(s.ldist, s.lid, sz, d, id);
       surv = !(r < sz && ((s.lid[r] ^ id) & kIdMask) == 0);
+      if (surv && p.visited)
+        surv = !visited_has(visited_table(p, blockIdx.x), p.visited_cap, p.visited_tag0 + s.misc[kMiscQid], id);
     }
     kd[e] = d;
     ki[e] = id;
@@ -762,6 +764,8 @@ __device__ __forceinline__ void merge_group(const SearchParams& p, const BSlot& 
     if (cand) {
       r = lower_bound_s(s.ldist, s.lid, sz, d, id);
       pre = !(r < sz && ((s.lid[r] ^ id) & kIdMask) == 0);
+      if (pre && p.visited)
+        pre = !visited_has(visited_table(p, blockIdx.x), p.visited_cap, p.visited_tag0 + s.misc[kMiscQid], id);
       if (pre) {
         s.sd[tid] = d;
         s.si[tid] = id;
@@ -933,6 +937,15 @@ __device__ int expand_block(const SearchParams& p, const BSlot& s, uint32_t mask
   constexpr int NV = MC > 0 ? MC / 16 : 1;
   const int tid = threadIdx.x;
   const int g = tid / RP, e = tid % RP;
+  if (p.visited) {  // visited mode: every node this pipe iteration expands is scheduled now
+    if (tid < kMaxPipeWidth && ((mask >> tid) & 1u) &&
+        !visited_insert(visited_table(p, blockIdx.x), p.visited_cap, p.visited_tag0 + s.misc[kMiscQid],
+                        static_cast<uint32_t>(s.lane[tid])) &&
+        atomicCAS(&s.misc[kMiscErr], 0, kErrVisited) == 0)
+      report_error(p, kErrVisited, qid, s.lane[tid], 0);
+    __syncthreads();
+    if (s.misc[kMiscErr]) return s.misc[kMiscErr];
+  }
   while (mask) {
     int ws[G], gact = 0;
 #pragma unroll

@@ -39,6 +39,7 @@ enum DeviceError : int32_t {
   kErrDegree = 2,         // stored degree > R
   kErrHopCap = 3,         // walk exceeded its iteration bound
   kErrNav = 4,            // nav graph: id out of range or entry search over its bound
+  kErrVisited = 5,        // visited-filter table full
 };
 
 // Byte offsets of one query slot's arrays inside the CTA's shared memory.
@@ -90,6 +91,11 @@ struct SearchParams {
   const int32_t* nav_graph;      // [nav_num_node x nav_max_m], -1 padded
   const int32_t* nav_mapping;    // [nav_num_node] nav id -> base id
   int32_t nav_num_node, nav_max_m, nav_start;
+  // visited-filter mode (not reference behaviour): per persistent CTA a
+  // table of visited_cap entries (tag << 32 | id); visited == nullptr: off
+  unsigned long long* visited;
+  int32_t visited_cap;           // power of two
+  uint32_t visited_tag0;         // tag of query qid = visited_tag0 + qid
   SlotLayout lay;
 };
 
@@ -384,6 +390,60 @@ __device__ __forceinline__ void report_error(const SearchParams& p, int code, in
   }
 }
 
+
+
+// ----------------------------------------------------------- visited mode
+// A mode of this build, off by default (the reference tracks visited nodes
+// only by bit 31 inside the candidate list, so a node that fell out of the
+// list can come back and be expanded again): each query keeps the nodes it
+// has scheduled for expansion in an open-addressing table of its CTA, in
+// global memory (L2-resident), and a new pair whose id is there never
+// re-enters the list.  Entries carry the query's tag, so the table is never
+// cleared between queries.
+
+__device__ __forceinline__ uint32_t visited_hash(uint32_t id) {
+  id ^= id >> 16;
+  id *= 0x85ebca6bu;
+  id ^= id >> 13;
+  id *= 0xc2b2ae35u;
+  return id ^ (id >> 16);
+}
+
+__device__ __forceinline__ unsigned long long* visited_table(const SearchParams& p, int slot) {
+  return p.visited + static_cast<size_t>(slot) * p.visited_cap;
+}
+
+// Returns false when the table is full (bounded probe).
+static __device__ __noinline__ bool visited_insert(unsigned long long* tab, int cap, uint32_t tag, uint32_t id) {
+  const unsigned long long want = (static_cast<unsigned long long>(tag) << 32) | id;
+  uint32_t h = visited_hash(id) & static_cast<uint32_t>(cap - 1);
+  for (int n = 0; n < cap; ++n) {
+    unsigned long long cur = __ldcg(tab + h);
+    for (int tries = 0; tries < 4; ++tries) {
+      if (static_cast<uint32_t>(cur >> 32) != tag) {  // empty or another query's entry: claim it
+        const unsigned long long old = atomicCAS(tab + h, cur, want);
+        if (old == cur) return true;
+        cur = old;
+        continue;
+      }
+      if (static_cast<uint32_t>(cur) == id) return true;
+      break;
+    }
+    h = (h + 1) & static_cast<uint32_t>(cap - 1);
+  }
+  return false;
+}
+
+static __device__ __noinline__ bool visited_has(const unsigned long long* tab, int cap, uint32_t tag, uint32_t id) {
+  uint32_t h = visited_hash(id) & static_cast<uint32_t>(cap - 1);
+  for (int n = 0; n < cap; ++n) {
+    const unsigned long long cur = __ldcg(tab + h);
+    if (static_cast<uint32_t>(cur >> 32) != tag) return false;
+    if (static_cast<uint32_t>(cur) == id) return true;
+    h = (h + 1) & static_cast<uint32_t>(cap - 1);
+  }
+  return false;
+}
 
 // ---------------------------------------------------------------- nav entry
 // The entry search of src/quiver/kernel_core/inkernel_nav.cuh:60-201: a

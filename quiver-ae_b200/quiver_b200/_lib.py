@@ -53,6 +53,7 @@ class SearchOpts(C.Structure):
         ("queries_per_block", C.c_int32), ("num_blocks", C.c_int32),
         ("early_exit_policy", C.c_int32), ("gpruning_warmup_steps", C.c_int32),
         ("gpruning_patience", C.c_int32), ("lut_mode", C.c_int32), ("skip_nav", C.c_int32),
+        ("visited_filter", C.c_int32),
     ]
 
 

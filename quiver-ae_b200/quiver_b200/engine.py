@@ -37,12 +37,13 @@ class SearchParams:
     gpruning_patience: int = 8
     lut_mode: int = _lib.QV_LUT_FP32
     skip_nav: bool = False   # True: entry = medoid even when the engine holds a nav graph
+    visited_filter: bool = False  # True: expanded nodes never re-enter the list (not reference behaviour)
 
     def to_c(self) -> _lib.SearchOpts:
         pol = {"none": _lib.QV_EXIT_NONE, "gpruning": _lib.QV_EXIT_GPRUNING}[self.early_exit_policy]
         return _lib.SearchOpts(self.topk, self.ef_search, self.pipe_width, self.queries_per_block,
                                self.num_blocks, pol, self.gpruning_warmup_steps, self.gpruning_patience,
-                               self.lut_mode, 1 if self.skip_nav else 0)
+                               self.lut_mode, 1 if self.skip_nav else 0, 1 if self.visited_filter else 0)
 
 
 class Engine:
