@@ -223,6 +223,8 @@ def main() -> int:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--latency", default="",
                     help="also time small batches end to end, e.g. 1,4,16 (latency mode; rank 0 only)")
+    ap.add_argument("--stripe-devices", default="",
+                    help="stripe the page store over these GPUs, e.g. 0,1 (pages p mod S; peer loads)")
     ap.add_argument("--visited-filter", action="store_true",
                     help="the engine's visited-filter mode (not reference behaviour; reports its recall)")
     ap.add_argument("--nav", action="store_true",
@@ -263,7 +265,11 @@ def main() -> int:
             workloads.prepare_nav(w, log=log)
     barrier()
     d = workloads.index_dir(w)
-    eng = Engine.open(d, w.data_type, device=local)
+    stripes = [int(x) for x in args.stripe_devices.split(",") if x]
+    if stripes:
+        eng = Engine.open(d, w.data_type, device=local, page_store="striped", stripe_devices=stripes)
+    else:
+        eng = Engine.open(d, w.data_type, device=local)
     nav_nodes = eng.nav_info[0] if args.nav else 0
 
     # ef calibration on the first CALIB_QUERIES rows (identical on every rank)
@@ -376,7 +382,8 @@ def main() -> int:
                        "early_exit": args.early_exit, "queries_per_step_per_gpu": nq,
                        "l2": f"inputs larger than L2: page store {info.num_pages * 4096 / 1e6:.0f} MB + codes "
                              f"{info.num_points * info.num_chunks / 1e6:.0f} MB vs 126 MB L2, no flush",
-                       "parallelism": f"query shards x{world}, index replicated"},
+                       "parallelism": f"query shards x{world}, index replicated",
+                       "page_store": f"striped over GPUs {stripes} (peer loads)" if stripes else "HBM of the search GPU"},
             "recall_at_10": recall, "p50_ms": p50, "p99_ms": p99,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": achieved / peaks["hbm_gbs"], "peak_source": peaks["source"],

@@ -43,6 +43,9 @@ extern "C" {
 /* Where the graph pages (vector + adjacency records) live. */
 #define QV_PAGES_HBM 0   /* device memory of the engine's GPU */
 #define QV_PAGES_HOST 1  /* pinned, mapped host DRAM read over PCIe */
+#define QV_PAGES_STRIPED 2  /* page p on stripe p mod S of S devices' HBM (S = 1, 2, 4 or 8, see
+                               qv_engine_opts.stripe_devices); the search GPU reads the other
+                               stripes with peer loads over NVLink / NVSwitch */
 
 /* Early-exit policy (src/quiver/io_control.cuh:41-46; the CLI accepts only
  * "none" and "gpruning", bin/quiver_search.cu:48-54). */
@@ -81,6 +84,9 @@ typedef struct {
   int32_t device;                 /* CUDA ordinal */
   int32_t page_store;             /* QV_PAGES_HBM or QV_PAGES_HOST */
   int32_t validate;               /* 1: check every adjacency list at load (degree <= R, ids < N) */
+  int32_t num_stripes;            /* QV_PAGES_STRIPED: S, a power of two <= 8 */
+  const int32_t* stripe_devices;  /* QV_PAGES_STRIPED: [S] CUDA ordinals (repeats allowed); every one
+                                     must be `device` or peer-accessible from it */
 } qv_engine_opts;
 
 /* Index arrays already in host memory, in the on-disk layouts:

@@ -67,6 +67,11 @@ struct qv_engine {
   int32_t M = 0;
   bool pages_host = false;
   uint8_t* d_pages = nullptr;   // what the kernel dereferences
+  // striped page store: stripe s on stripe_dev[s]; stripe_table lives on `device`
+  std::vector<int> stripe_dev;
+  std::vector<uint8_t*> stripe_ptr;
+  uint8_t** d_stripe_table = nullptr;
+  int stripe_shift = 0;
   uint8_t* h_pages = nullptr;   // pinned mapped host allocation (host store)
   uint8_t* d_codes = nullptr;
   float* d_pivots_t = nullptr;
@@ -105,9 +110,16 @@ struct qv_engine {
       if (p) cudaFree(p);
     if (pages_host) {
       if (h_pages) cudaFreeHost(h_pages);
-    } else if (d_pages) {
+    } else if (d_pages && stripe_ptr.empty()) {  // with stripes, d_pages is stripe 0
       cudaFree(d_pages);
     }
+    for (size_t s = 0; s < stripe_ptr.size(); ++s) {
+      if (!stripe_ptr[s]) continue;
+      cudaSetDevice(stripe_dev[s]);
+      cudaFree(stripe_ptr[s]);
+    }
+    if (device >= 0) cudaSetDevice(device);
+    if (d_stripe_table) cudaFree(d_stripe_table);
     for (auto& e : ev)
       if (e) cudaEventDestroy(e);
     if (stream) cudaStreamDestroy(stream);
@@ -227,6 +239,8 @@ qvk::SearchParams make_params(const qv_engine* e, const Plan& pl, const qv_searc
                               int32_t* found, int32_t* steps, int64_t* nbrs, int64_t* times = nullptr) {
   qvk::SearchParams p{};
   p.pages = e->d_pages;
+  p.stripe_table = reinterpret_cast<const unsigned long long*>(e->d_stripe_table);
+  p.stripe_shift = e->stripe_shift;
   p.codes = e->d_codes;
   p.pivots_t = e->d_pivots_t;
   p.centroid = e->d_centroid;
@@ -381,9 +395,54 @@ void alloc_pages(qv_engine* e, int32_t page_store) {
     CK(cudaHostGetDevicePointer(reinterpret_cast<void**>(&e->d_pages), e->h_pages, 0));
   } else if (page_store == QV_PAGES_HBM) {
     CK(cudaMalloc(&e->d_pages, bytes));
-  } else {
-    fail(QV_ERR_INVALID_ARG, "page_store must be QV_PAGES_HBM or QV_PAGES_HOST");
+  } else if (page_store != QV_PAGES_STRIPED) {
+    fail(QV_ERR_INVALID_ARG, "page_store must be QV_PAGES_HBM, QV_PAGES_HOST or QV_PAGES_STRIPED");
   }
+}
+
+// Striped page store: page p goes to stripe p & (S - 1) at local page
+// p >> log2(S); stripes on other devices are read by peer loads, so peer
+// access from the search device is enabled for each of them.
+void stripe_pages(qv_engine* e, const uint8_t* host_pages, int32_t num_stripes, const int32_t* devices) {
+  if (num_stripes < 1 || num_stripes > 8 || (num_stripes & (num_stripes - 1)) != 0 || !devices)
+    fail(QV_ERR_INVALID_ARG, "num_stripes must be 1, 2, 4 or 8, with stripe_devices");
+  int count = 0;
+  CK(cudaGetDeviceCount(&count));
+  for (int s = 0; s < num_stripes; ++s)
+    if (devices[s] < 0 || devices[s] >= count) fail(QV_ERR_INVALID_ARG, "stripe device ordinal out of range");
+  for (int s = 0; s < num_stripes; ++s) {
+    const int d = devices[s];
+    if (d == e->device) continue;
+    int can = 0;
+    CK(cudaDeviceCanAccessPeer(&can, e->device, d));
+    if (!can)
+      fail(QV_ERR_UNSUPPORTED, "device " + std::to_string(d) + " is not peer-accessible from device " +
+                                   std::to_string(e->device));
+    const cudaError_t pe = cudaDeviceEnablePeerAccess(d, 0);  // current device: e->device
+    if (pe == cudaErrorPeerAccessAlreadyEnabled) cudaGetLastError();
+    else if (pe != cudaSuccess) CK(pe);
+  }
+  int shift = 0;
+  while ((1 << shift) < num_stripes) ++shift;
+  const int64_t P = e->L.num_pages;
+  e->stripe_dev.assign(devices, devices + num_stripes);
+  e->stripe_ptr.assign(num_stripes, nullptr);
+  std::vector<uint8_t> gather;
+  for (int s = 0; s < num_stripes; ++s) {
+    const int64_t n = P > s ? (P - s + num_stripes - 1) / num_stripes : 0;
+    gather.resize(static_cast<size_t>(std::max<int64_t>(n, 1)) * qv::kPage);
+    for (int64_t j = 0; j < n; ++j)
+      std::memcpy(gather.data() + static_cast<size_t>(j) * qv::kPage,
+                  host_pages + static_cast<size_t>(j * num_stripes + s) * qv::kPage, qv::kPage);
+    CK(cudaSetDevice(e->stripe_dev[s]));
+    CK(cudaMalloc(&e->stripe_ptr[s], gather.size()));
+    CK(cudaMemcpy(e->stripe_ptr[s], gather.data(), static_cast<size_t>(n) * qv::kPage, cudaMemcpyHostToDevice));
+  }
+  CK(cudaSetDevice(e->device));
+  CK(cudaMalloc(&e->d_stripe_table, sizeof(uint8_t*) * num_stripes));
+  CK(cudaMemcpy(e->d_stripe_table, e->stripe_ptr.data(), sizeof(uint8_t*) * num_stripes, cudaMemcpyHostToDevice));
+  e->stripe_shift = shift;
+  e->d_pages = e->stripe_ptr[0];  // stripe 0 (the whole store when S == 1)
 }
 
 void ensure_staging(qv_engine* e, int64_t nq, int64_t k) {
@@ -446,8 +505,7 @@ __global__ void l2_component_kernel(const qvk::SearchParams p, const float* q2, 
   const int64_t i = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   if (i >= n) return;
   const int64_t v = ids[i];
-  const T* vec = reinterpret_cast<const T*>(p.pages + (v / p.npp) * qvk::kPageSize +
-                                            (v % p.npp) * p.node_size);
+  const T* vec = reinterpret_cast<const T*>(qvk::node_record(p, static_cast<uint32_t>(v)));
   const float d = qvk::exact_l2_warp<T>(q2 + static_cast<int64_t>(qof[i]) * p.dim, vec, p.dim, lane);
   if (lane == 0) out[i] = d;
 }
@@ -535,7 +593,10 @@ int qv_engine_create(const qv_engine_opts* opts, qv_engine** out) {
         const int64_t b = qv::validate_adjacency(e->L, host.data());
         if (b >= 0) fail(QV_ERR_BAD_INDEX, "adjacency list of node " + std::to_string(b) + " is malformed");
       }
-      CK(cudaMemcpy(e->d_pages, host.data(), bytes, cudaMemcpyHostToDevice));
+      if (opts->page_store == QV_PAGES_STRIPED)
+        stripe_pages(e.get(), host.data(), opts->num_stripes, opts->stripe_devices);
+      else
+        CK(cudaMemcpy(e->d_pages, host.data(), bytes, cudaMemcpyHostToDevice));
     }
     upload_pq(e.get(), pq.pivots.data(), pq.centroid.data(), pq.chunk_offsets.data(), pq.codes.data());
     // search_setup.hpp:96-105: a nav graph next to the index is used when present
@@ -573,6 +634,8 @@ int qv_engine_create_from_arrays(const qv_index_arrays* a, int32_t device, int32
     shape.chunk_offsets.assign(a->chunk_offsets, a->chunk_offsets + in.num_chunks + 1);
     qv::check_layout(e->L, &shape);
     init_device_side(e.get(), device);
+    if (page_store == QV_PAGES_STRIPED)
+      fail(QV_ERR_UNSUPPORTED, "a striped page store is created from an index directory (qv_engine_create)");
     alloc_pages(e.get(), page_store);
     const size_t bytes = static_cast<size_t>(e->L.num_pages) * qv::kPage;
     if (e->pages_host)
@@ -887,6 +950,8 @@ int qv_exact_l2_device(qv_engine* e, const float* d_q2, const int32_t* d_qof, co
     if (n <= 0) return;
     qvk::SearchParams p{};
     p.pages = e->d_pages;
+    p.stripe_table = reinterpret_cast<const unsigned long long*>(e->d_stripe_table);
+    p.stripe_shift = e->stripe_shift;
     p.dim = static_cast<int32_t>(e->L.dim);
     p.npp = static_cast<int32_t>(e->L.nodes_per_page);
     p.node_size = static_cast<int32_t>(e->L.node_size);

@@ -165,11 +165,7 @@ __device__ __forceinline__ void build_lut_block(const SearchParams& p, const flo
   __syncthreads();
 }
 
-// Node v's record in the page store (ids are below 2^31, so 32-bit division).
-__device__ __forceinline__ const uint8_t* record_ptr(const SearchParams& p, uint32_t v) {
-  const uint32_t npp = static_cast<uint32_t>(p.npp);
-  return p.pages + static_cast<size_t>(v / npp) * kPageSize + static_cast<size_t>(v % npp) * p.node_size;
-}
+__device__ __forceinline__ const uint8_t* record_ptr(const SearchParams& p, uint32_t v) { return node_record(p, v); }
 
 // The last warp of each active group scores the group's node exactly
 // (square_sum_32 order: lane l accumulates dims l, l + 32, ... with fused

@@ -65,7 +65,12 @@ struct SlotLayout {
 };
 
 struct SearchParams {
-  const uint8_t* pages;          // page store: page p at pages + p * 4096
+  const uint8_t* pages;          // page store: page p at pages + p * 4096 (stripe_shift == 0)
+  // striped page store (stripe_shift > 0): page p is page p >> stripe_shift of
+  // stripe p & (2^stripe_shift - 1), whose base (possibly another GPU's
+  // memory, read over NVLink) is stripe_table[stripe]
+  const unsigned long long* stripe_table;  // stripe base addresses
+  int32_t stripe_shift;
   const uint8_t* codes;          // [N x M] PQ codes
   const float* pivots_t;         // [dim x 256]
   const float* centroid;         // [dim]
@@ -569,6 +574,19 @@ __device__ int32_t nav_entry_warp(const SearchParams& p, const float* q, uint32_
   return entry;
 }
 
+// Node v's record in the page store: page v / npp at offset (v % npp) *
+// node_size (search.cu:240, kernel_helpers.cuh:257); ids are below 2^31, so
+// 32-bit division.
+__device__ __forceinline__ const uint8_t* node_record(const SearchParams& p, uint32_t v) {
+  const uint32_t npp = static_cast<uint32_t>(p.npp);
+  const uint32_t page = v / npp;
+  const size_t off = static_cast<size_t>(v % npp) * p.node_size;
+  if (p.stripe_shift == 0) return p.pages + static_cast<size_t>(page) * kPageSize + off;
+  const uint8_t* base =
+      reinterpret_cast<const uint8_t*>(__ldg(p.stripe_table + (page & ((1u << p.stripe_shift) - 1u))));
+  return base + static_cast<size_t>(page >> p.stripe_shift) * kPageSize + off;
+}
+
 __device__ __forceinline__ uint32_t code_byte(const uint4& v, int b) {
   const uint32_t w = (b < 4) ? v.x : (b < 8) ? v.y : (b < 12) ? v.z : v.w;
   return (w >> ((b & 3) * 8)) & 0xffu;
@@ -613,8 +631,7 @@ __device__ int expand_lanes(const SearchParams& p, const Slot& s, QueryState& q,
       for (int t = 0; t < SMAX; ++t) nb[g][t] = 0;
       if (g < gact) {
         const int64_t v = node[g];
-        const uint32_t* rec = reinterpret_cast<const uint32_t*>(
-            p.pages + (v / p.npp) * kPageSize + (v % p.npp) * p.node_size);
+        const uint32_t* rec = reinterpret_cast<const uint32_t*>(node_record(p, static_cast<uint32_t>(v)));
         deg[g] = rec[p.data_words];
 #pragma unroll
         for (int t = 0; t < SMAX; ++t) {

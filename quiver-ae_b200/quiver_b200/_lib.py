@@ -12,7 +12,7 @@ from . import _build
 
 QV_OK = 0
 QV_UINT8, QV_FLOAT, QV_INT8 = 0, 1, 2
-QV_PAGES_HBM, QV_PAGES_HOST = 0, 1
+QV_PAGES_HBM, QV_PAGES_HOST, QV_PAGES_STRIPED = 0, 1, 2
 QV_EXIT_NONE, QV_EXIT_GPRUNING = 0, 2
 QV_LUT_FP32 = 0
 
@@ -36,7 +36,7 @@ class EngineOpts(C.Structure):
     _fields_ = [
         ("index_dir", C.c_char_p), ("data_type", C.c_int32), ("memory_backend", C.c_char_p),
         ("memory_index_file", C.c_char_p), ("device", C.c_int32), ("page_store", C.c_int32),
-        ("validate", C.c_int32),
+        ("validate", C.c_int32), ("num_stripes", C.c_int32), ("stripe_devices", C.c_void_p),
     ]
 
 

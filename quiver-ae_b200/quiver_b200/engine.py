@@ -56,12 +56,16 @@ class Engine:
     @classmethod
     def open(cls, index_dir: str | Path, data_type: str = "uint8", *, memory_backend: str = "heap",
              memory_index_file: str | None = None, device: int = 0, page_store: str = "hbm",
-             validate: bool = False) -> "Engine":
+             validate: bool = False, stripe_devices: list[int] | None = None) -> "Engine":
+        """page_store: "hbm", "host" (pinned mapped DRAM) or "striped" (page p on
+        stripe_devices[p % len(stripe_devices)], read by peer loads)."""
         lib = _lib.engine_lib()
+        devs = np.ascontiguousarray(stripe_devices or [], dtype=np.int32)
         opts = _lib.EngineOpts(str(index_dir).encode(), _lib.DTYPE_CODES[data_type], memory_backend.encode(),
                                memory_index_file.encode() if memory_index_file else None, device,
-                               {"hbm": _lib.QV_PAGES_HBM, "host": _lib.QV_PAGES_HOST}[page_store],
-                               1 if validate else 0)
+                               {"hbm": _lib.QV_PAGES_HBM, "host": _lib.QV_PAGES_HOST,
+                                "striped": _lib.QV_PAGES_STRIPED}[page_store],
+                               1 if validate else 0, len(devs), C.c_void_p(devs.ctypes.data) if len(devs) else None)
         h = C.c_void_p()
         _check(lib.qv_engine_create(C.byref(opts), C.byref(h)))
         return cls(h)
