@@ -241,6 +241,25 @@ int qv_adc_device(qv_engine* engine, const float* d_lut, const int32_t* d_query_
 int qv_exact_l2_device(qv_engine* engine, const float* d_q2, const int32_t* d_query_of,
                        const int32_t* d_ids, int64_t n, float* d_out, void* stream);
 
+/* Batched ADC over raw device buffers, no engine needed: query q scores
+ * n_per_query codes with its LUT d_luts[q] ([M x 256] fp32, the layout
+ * PQSearchData::init_query writes, pq_device.cuh:9-36), summing the M lookups
+ * in chunk order like the search's scoring loop (kernel_helpers.cuh:271-286):
+ *   d_out[q * n + i] = sum_j d_luts[q][j][code(id)[j]]
+ * where id = d_ids[q * n + i] (a gather), or, with d_ids NULL,
+ * id = d_first[q] + i (a contiguous range).  An id outside [0, num_points)
+ * gives NaN and is not read.  d_codes is [num_points x M] uint8; M must be a
+ * multiple of 4 and d_luts 16-byte aligned.  kernel picks the implementation:
+ * QV_ADC_PIPE (M == 32, 16-byte aligned codes; for thousands of codes per
+ * query), QV_ADC_THREAD (any M), or QV_ADC_AUTO.  Asynchronous on stream. */
+#define QV_ADC_AUTO 0
+#define QV_ADC_THREAD 1
+#define QV_ADC_PIPE 2
+int qv_adc_batch(const uint8_t* d_codes, int64_t num_points, int32_t M,
+                 const float* d_luts, int64_t nq, const int32_t* d_ids,
+                 const int64_t* d_first, int64_t n_per_query, float* d_out,
+                 int32_t kernel, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -226,6 +226,23 @@ def adc(lut: np.ndarray, code: np.ndarray) -> float:
     return float(np.float32(lib().orc_adc(lut.ctypes.data, code.ctypes.data, code.shape[0])))
 
 
+def adc_batch(luts: np.ndarray, codes: np.ndarray, ids: np.ndarray) -> np.ndarray:
+    """dist[q, i] = sum_j luts[q, j, codes[ids[q, i], j]], summed in chunk order j = 0..M-1 in fp32
+    (the scoring loop of src/shared/kernel_helpers.cuh:271-286, vectorised over pairs: each numpy
+    float32 add rounds like the scalar loop's).  Ids outside [0, len(codes)) give NaN."""
+    luts = np.asarray(luts, dtype=np.float32)
+    nq, M = luts.shape[0], codes.shape[1]
+    luts = luts.reshape(nq, M, 256)
+    ids = np.asarray(ids, dtype=np.int64).reshape(nq, -1)
+    ok = (ids >= 0) & (ids < codes.shape[0])
+    safe = np.where(ok, ids, 0)
+    qi = np.arange(nq)[:, None]
+    acc = np.zeros(ids.shape, dtype=np.float32)
+    for j in range(M):
+        acc = acc + luts[qi, j, codes[safe, j]]
+    return np.where(ok, acc, np.float32(np.nan)).astype(np.float32)
+
+
 def exact_l2(ix: OracleIndex, q2: np.ndarray, v: int) -> float:
     q2 = np.ascontiguousarray(q2, dtype=np.float32)
     vec = np.ascontiguousarray(ix.vector(v))

@@ -520,6 +520,14 @@ const char* qv_version(void) { return "quiver-b200 0.1.0 (sm_100a)"; }
 
 const char* qv_last_error(void) { return g_last_error.c_str(); }
 
+}  // extern "C"
+
+namespace qv {
+void set_last_error(const std::string& m) { g_last_error = m; }
+}  // namespace qv
+
+extern "C" {
+
 void qv_search_opts_default(qv_search_opts* o) {
   if (!o) return;
   o->topk = 10;

@@ -15,6 +15,7 @@ QV_UINT8, QV_FLOAT, QV_INT8 = 0, 1, 2
 QV_PAGES_HBM, QV_PAGES_HOST, QV_PAGES_STRIPED = 0, 1, 2
 QV_EXIT_NONE, QV_EXIT_GPRUNING = 0, 2
 QV_LUT_FP32 = 0
+QV_ADC_AUTO, QV_ADC_THREAD, QV_ADC_PIPE = 0, 1, 2
 
 DTYPE_CODES = {"uint8": QV_UINT8, "float": QV_FLOAT, "float32": QV_FLOAT, "int8": QV_INT8}
 
@@ -94,6 +95,8 @@ ENGINE_SYMBOLS = {
     "qv_adc_device": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_void_p, C.c_void_p]),
     "qv_exact_l2_device": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_void_p,
                                      C.c_void_p]),
+    "qv_adc_batch": (C.c_int, [C.c_void_p, C.c_int64, C.c_int32, C.c_void_p, C.c_int64, C.c_void_p, C.c_void_p,
+                               C.c_int64, C.c_void_p, C.c_int32, C.c_void_p]),
 }
 
 INDEX_SYMBOLS = {
