@@ -209,6 +209,62 @@ def cpu_baseline(w, d, ef: int, args) -> dict:
             "sample": f"first {n} of the {w.nq} step queries, ef_search={ef}, {dt:.1f} s of host work"}
 
 
+ADC_POINTS, ADC_QUERIES, ADC_PER_QUERY = 100_000_000, 2048, 65_536
+# (mode, kernel, algorithmic bytes per pair): 32 code + 4 distance written, + 4 id read for gathers
+ADC_DEFAULT = (("stream", "pipe", 36), ("gather", "thread", 40))
+ADC_ALL = (("stream", "pipe", 36), ("stream", "thread", 36), ("gather", "thread", 40), ("gather", "pipe", 40))
+
+
+def adc_microbench(dev, stream, peak_gbs: float, points: int = ADC_POINTS, queries: int = ADC_QUERIES,
+                   per_query: int = ADC_PER_QUERY, reps: int = 10, combos=ADC_DEFAULT) -> dict:
+    """Batched ADC (qv_adc_batch) over `points` x 32-byte codes in HBM (100M = 3.2 GB, config 2's code
+    array, by default): `queries` x `per_query` codes, as contiguous ranges (stream) and as uniformly random
+    ids (gather).  Every combination is warmed up (3 launches each, in order) before any is timed, then each
+    is timed over `reps` launches with CUDA events on `stream`."""
+    import torch
+    from quiver_b200.adc import adc_batch
+    g = torch.Generator(device=dev).manual_seed(7)
+    codes = torch.empty((points, 32), dtype=torch.uint8, device=dev)
+    step = 10_000_000
+    for i in range(0, points, step):
+        codes[i:i + step] = torch.randint(0, 256, (min(step, points - i), 32), dtype=torch.uint8, device=dev,
+                                          generator=g)
+    luts = torch.rand((queries, 32, 256), device=dev, generator=g) * 4096.0
+    first = (torch.arange(queries, device=dev, dtype=torch.int64) * per_query) % (points - per_query)
+    ids = torch.randint(0, points, (queries, per_query), dtype=torch.int32, device=dev, generator=g)
+    out = torch.empty((queries, per_query), dtype=torch.float32, device=dev)
+    pairs = queries * per_query
+    res = {"workload": f"{points / 1e6:g}M codes x 32 B in HBM ({points * 32 / 1e9:.2f} GB), {queries} queries x "
+                       f"{per_query} codes, fp32 LUTs, chunk-ordered sums",
+           "peak_gbs": peak_gbs}
+
+    def run(mode, kernel):
+        if mode == "stream":
+            adc_batch(codes, luts, first=first, n_per_query=per_query, out=out, kernel=kernel, stream=stream)
+        else:
+            adc_batch(codes, luts, ids, out=out, kernel=kernel, stream=stream)
+
+    for mode, kernel, _ in combos:
+        for _ in range(3):
+            run(mode, kernel)
+    for mode, kernel, per_pair in combos:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            run(mode, kernel)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / reps
+        gbs = pairs * per_pair / (ms / 1e3) / 1e9
+        key = mode if combos is ADC_DEFAULT else f"{mode}_{kernel}"
+        res[key] = {"kernel": f"adc_{kernel}", "ms_per_launch": ms, "gpairs_per_s": pairs / (ms / 1e3) / 1e9,
+                    "alg_bytes_per_pair": per_pair, "achieved_gbs": gbs, "frac": gbs / peak_gbs,
+                    "code_gbs": pairs * 32 / (ms / 1e3) / 1e9}
+    del codes, luts, first, ids, out
+    torch.cuda.empty_cache()
+    return res
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -229,6 +285,13 @@ def main() -> int:
                     help="the engine's visited-filter mode (not reference behaviour; reports its recall)")
     ap.add_argument("--nav", action="store_true",
                     help="start each query from the nav-graph entry search (a 1 %% nav graph is built and cached)")
+    ap.add_argument("--no-adc", action="store_true",
+                    help="skip the batched-ADC measurement (adc_batch object of the JSON line)")
+    ap.add_argument("--adc-only", action="store_true",
+                    help="run only the batched-ADC measurement, every kernel on both access patterns")
+    ap.add_argument("--adc-points", type=int, default=ADC_POINTS)
+    ap.add_argument("--adc-queries", type=int, default=ADC_QUERIES)
+    ap.add_argument("--adc-reps", type=int, default=10)
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -250,6 +313,13 @@ def main() -> int:
 
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
+    if args.adc_only:
+        if rank == 0:
+            stream = torch.cuda.Stream(dev)
+            res = adc_microbench(dev, stream, read_peaks()["hbm_gbs"], points=args.adc_points,
+                                 queries=args.adc_queries, reps=args.adc_reps, combos=ADC_ALL)
+            print(json.dumps({"adc_batch": res}), flush=True)
+        return 0
     if world > 1:
         dist.init_process_group("nccl", timeout=timedelta(seconds=900), device_id=dev)
 
@@ -400,6 +470,8 @@ def main() -> int:
                                            "(H2D, one kernel, D2H, sync), same ef / pipe width"}
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(w, d, ef, args)
+        if not args.no_adc:
+            line["adc_batch"] = adc_microbench(dev, stream, peaks["hbm_gbs"])
         print(json.dumps(line), flush=True)
     eng.close()
     if world > 1:

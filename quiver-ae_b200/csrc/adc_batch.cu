@@ -397,10 +397,10 @@ extern "C" int qv_adc_batch(const uint8_t* d_codes, int64_t num_points, int32_t 
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, threads, smem) != cudaSuccess || per_sm < 1)
     return fail(QV_ERR_CUDA, "qv_adc_batch: kernel does not fit on an SM");
   const int64_t slots = static_cast<int64_t>(per_sm) * sms;
-  // Split queries into work items so every resident CTA has work; keep items long enough that staging the
-  // LUT is a small share of an item.
+  // Split queries into work items: about eight waves of items over the resident CTAs keeps the last wave's
+  // idle share small, and items long enough that staging the LUT is a small share of an item.
   const int64_t min_chunk = pipe ? 8192 : 2048;
-  int64_t nchunk = std::max<int64_t>(1, (2 * slots + nq - 1) / nq);
+  int64_t nchunk = std::max<int64_t>(1, (8 * slots + nq - 1) / nq);
   nchunk = std::min<int64_t>(nchunk, std::max<int64_t>(1, n_per_query / min_chunk));
   const int64_t chunk = (n_per_query + nchunk - 1) / nchunk;
   nchunk = (n_per_query + chunk - 1) / chunk;
