@@ -401,9 +401,24 @@ def main() -> int:
     barrier()
     value = world * args.steps * nq / (total_ms / 1000.0)
 
-    # per-query service latency at the same operating point
+    # per-query service latency at the same operating point (kernel timer: bind to finish)
     lat = eng.search_timed(q, p)[3]
     p50, p99 = float(np.percentile(lat, 50)), float(np.percentile(lat, 99))
+
+    # streaming admission: the reference's host loop and its QueryLatency(ms)
+    # (admission to observed completion); the call with the median QPS of 5
+    streaming = None
+    if rank == 0:
+        eng.search_stream(q, p)
+        runs = sorted((eng.search_stream(q, p)[4] for _ in range(5)), key=lambda st: st.qps)
+        st = runs[len(runs) // 2]
+        streaming = {"qps": st.qps, "lat_avg_ms": st.lat_avg_ms, "p50_ms": st.lat_p50_ms, "p90_ms": st.lat_p90_ms,
+                     "p99_ms": st.lat_p99_ms, "p999_ms": st.lat_p999_ms, "max_ms": st.lat_max_ms,
+                     "workers": st.workers, "max_inflight": st.max_inflight, "admissions": st.admissions,
+                     "queries": nq,
+                     "how": "qv_search_stream: one persistent launch, host admits ranges as completions allow "
+                            "(prefeed = workers, admit_min_batch 32); latency = host time from a query's "
+                            "admission to the completion count passing it; median-QPS call of 5"}
 
     # end to end through the C ABI with pinned host buffers
     hq = torch.from_numpy(q).pin_memory()
@@ -454,7 +469,14 @@ def main() -> int:
                              f"{info.num_points * info.num_chunks / 1e6:.0f} MB vs 126 MB L2, no flush",
                        "parallelism": f"query shards x{world}, index replicated",
                        "page_store": f"striped over GPUs {stripes} (peer loads)" if stripes else "HBM of the search GPU"},
-            "recall_at_10": recall, "p50_ms": p50, "p99_ms": p99,
+            "recall_at_10": recall,
+            "p50_ms": streaming["p50_ms"] if streaming else None,
+            "p99_ms": streaming["p99_ms"] if streaming else None,
+            "latency_definition": "QueryLatency(ms) of the streaming admission loop (see streaming)",
+            "streaming": streaming,
+            "service_latency": {"p50_ms": p50, "p99_ms": p99,
+                                "how": "kernel global timer from a worker binding the query to its results, "
+                                       "every query admitted at the call (qv_search_timed)"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": achieved / peaks["hbm_gbs"], "peak_source": peaks["source"],
                          "traffic": traffic, "algorithmic_bytes_per_launch": alg_bytes,

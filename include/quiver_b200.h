@@ -191,6 +191,44 @@ int qv_search_timed(qv_engine* engine, const float* queries, int64_t nq, int64_t
                     const qv_search_opts* opts, int32_t* ids, float* dists,
                     int32_t* found, float* query_ms, qv_search_stats* stats);
 
+/* Streaming admission: the reference's run_persistent_search host loop
+ * (src/quiver/search.cu:820-1198).  One persistent launch serves all nq
+ * queries while the host admits them in order: the first
+ * min(workers + prefeed, nq) before the launch, then, whenever completions
+ * allow (in flight <= workers + prefeed), the next range -- at least
+ * admit_min_batch queries unless it is the last range or nothing is pending
+ * -- copied host-to-device on a second stream and made visible to the kernel
+ * in stream order after the copy.  A worker that binds a query not yet fed
+ * waits for it (at most feed_timeout_ms; then the call fails with
+ * QV_ERR_DEVICE).  Latency follows the reference's QueryLatency(ms): the i-th
+ * completion the host observes is charged to the i-th admitted query, from
+ * the host time its admission started (the call's start for the first range)
+ * to the time the host saw the completion count pass i.  Results equal
+ * qv_search's bit for bit.  The caller's query array is page-locked for the
+ * call (cudaHostRegister), as the reference does. */
+typedef struct qv_stream_opts {
+  int32_t prefeed;          /* admitted queries beyond the workers; < 0: as many as workers */
+  int32_t admit_min_batch;  /* smallest admission while one is pending (reference: 32) */
+  int32_t feed_timeout_ms;  /* bound on a worker's wait for its query */
+  int32_t admit_limit;      /* admit at most this many queries (< 0: all); a test hook for the timeout */
+} qv_stream_opts;
+void qv_stream_opts_default(qv_stream_opts* opts);
+
+typedef struct qv_stream_stats {
+  double search_ms;         /* call start (before the first copy) to the last completion seen */
+  double qps;               /* nq / search_ms */
+  double lat_avg_ms, lat_p50_ms, lat_p90_ms, lat_p99_ms, lat_p999_ms, lat_max_ms;
+  int64_t admissions;       /* host-to-device ranges submitted, the first included */
+  int32_t workers;          /* CTAs (block kernel) or warps (warp kernel) of the launch */
+  int32_t max_inflight;     /* workers + prefeed */
+  int64_t expansions;       /* nodes expanded, all queries */
+} qv_stream_stats;
+
+int qv_search_stream(qv_engine* engine, const float* queries, int64_t nq, int64_t dim,
+                     const qv_search_opts* opts, const qv_stream_opts* sopts,
+                     int32_t* ids, float* dists, int32_t* found,
+                     float* query_latency_ms, qv_stream_stats* stats);
+
 /* Same search with DEVICE buffers on the engine's GPU, enqueued on `stream`
  * (a cudaStream_t; NULL = the engine's own stream, cudaStreamLegacy for the
  * legacy default stream) without a host

@@ -36,6 +36,11 @@ struct Args {
   std::string memory_backend = "heap", memory_index_file, num_blocks_list, result_prefix;
   std::string early_exit_policy = "gpruning", step_recall_csv = "quiver_step_recall.csv", final_recall_csv;
   std::string page_store = "hbm";
+  // stream: one persistent launch with the host admitting queries as they
+  // complete (the reference's host loop, search.cu:983-1051); batch: every
+  // query admitted at the call
+  std::string admission = "stream";
+  int prefeed = -1, admit_min_batch = 32;
   int topk = 10, ef_search = 30, repeat = 20;
   int num_blocks = 756, poll_threads = 6, pipe_width = 2, queries_per_block = 1, runners_per_ssd = 1;
   int device = 0;
@@ -50,7 +55,8 @@ const char* kUsage =
     "  [--num-blocks 756] [--num-blocks-list LIST] [--queries-per-block 1] [--pipe-width 2]\n"
     "  [--poll-threads 6] [--runners-per-ssd 1] [--early-exit-policy gpruning|none]\n"
     "  [--result-prefix PREFIX] [--final-recall-csv FILE] [--skip-nav]\n"
-    "  [--page-store hbm|host] [--device N]\n";
+    "  [--page-store hbm|host] [--device N]\n"
+    "  [--admission stream|batch] [--prefeed N] [--admit-min-batch N]\n";
 
 bool parse_int(const std::string& flag, const std::string& v, int& out) {
   try {
@@ -65,18 +71,22 @@ bool parse_int(const std::string& flag, const std::string& v, int& out) {
 }
 
 int parse_args(int argc, char** argv, Args& a) {
+  // the reference reads these from the environment (search.cu:829-831, 975-977)
+  if (const char* v = std::getenv("QUIVER_PREFEED")) a.prefeed = std::atoi(v);
+  if (const char* v = std::getenv("QUIVER_ADMIT_MIN_BATCH")) a.admit_min_batch = std::max(1, std::atoi(v));
   std::map<std::string, std::string*> str = {
       {"--index-dir", &a.index_dir}, {"--query", &a.query_file}, {"--ground-truth", &a.ground_truth_file},
       {"--data-type", &a.data_type}, {"--ssd-list-file", &a.ssd_list_file},
       {"--memory-backend", &a.memory_backend}, {"--memory-index-file", &a.memory_index_file},
       {"--num-blocks-list", &a.num_blocks_list}, {"--result-prefix", &a.result_prefix},
       {"--early-exit-policy", &a.early_exit_policy}, {"--step-recall-csv", &a.step_recall_csv},
-      {"--final-recall-csv", &a.final_recall_csv}, {"--page-store", &a.page_store}};
+      {"--final-recall-csv", &a.final_recall_csv}, {"--page-store", &a.page_store},
+      {"--admission", &a.admission}};
   std::map<std::string, int*> ints = {
       {"--topk", &a.topk}, {"--ef-search", &a.ef_search}, {"--repeat", &a.repeat},
       {"--num-blocks", &a.num_blocks}, {"--poll-threads", &a.poll_threads}, {"--pipe-width", &a.pipe_width},
       {"--queries-per-block", &a.queries_per_block}, {"--runners-per-ssd", &a.runners_per_ssd},
-      {"--device", &a.device}};
+      {"--device", &a.device}, {"--prefeed", &a.prefeed}, {"--admit-min-batch", &a.admit_min_batch}};
   int ignored = 0;
   std::map<std::string, int*> ignored_ints = {{"--spdk-submit-queue-cap", &ignored},
                                               {"--spdk-task-contexts", &ignored},
@@ -119,6 +129,10 @@ int parse_args(int argc, char** argv, Args& a) {
       std::cerr << "Unknown argument: " << flag << std::endl << kUsage;
       return 1;
     }
+  }
+  if (a.admission != "stream" && a.admission != "batch") {
+    std::cerr << "--admission must be stream or batch" << std::endl;
+    return 1;
   }
   for (auto req : {std::make_pair("--index-dir", &a.index_dir), std::make_pair("--query", &a.query_file),
                    std::make_pair("--data-type", &a.data_type)}) {
@@ -359,38 +373,78 @@ int main(int argc, char** argv) {
     so.num_blocks = nb;
     so.early_exit_policy = policy;
     so.skip_nav = a.skip_nav ? 1 : 0;
-    qv_search_stats st{};
-    const auto t0 = std::chrono::steady_clock::now();
-    if (qv_search_timed(eng, queries.data(), static_cast<int64_t>(nq), info.dim, &so, ids.data(), dists.data(),
-                        found.data(), lat.data(), &st) != QV_OK) {
+    qv_search_stats plan{};
+    if (qv_plan(eng, &so, static_cast<int64_t>(nq), &plan) != QV_OK) {
       std::cerr << qv_last_error() << std::endl;
       qv_engine_destroy(eng);
       return 1;
     }
-    const double secs = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
-    std::vector<double> l(lat.begin(), lat.end());
-    std::sort(l.begin(), l.end());
-    const double avg = l.empty() ? 0.0 : std::accumulate(l.begin(), l.end(), 0.0) / l.size();
+    double qps = 0, avg = 0, p50 = 0, p90 = 0, p99 = 0, p999 = 0, lmax = 0;
+    int64_t expansions = 0;
+    std::string admission_params;
+    if (a.admission == "stream") {
+      qv_stream_opts sto;
+      qv_stream_opts_default(&sto);
+      sto.prefeed = a.prefeed;
+      sto.admit_min_batch = std::max(1, a.admit_min_batch);
+      qv_stream_stats ss{};
+      if (qv_search_stream(eng, queries.data(), static_cast<int64_t>(nq), info.dim, &so, &sto, ids.data(),
+                           dists.data(), found.data(), nullptr, &ss) != QV_OK) {
+        std::cerr << qv_last_error() << std::endl;
+        qv_engine_destroy(eng);
+        return 1;
+      }
+      qps = ss.qps;
+      avg = ss.lat_avg_ms;
+      p50 = ss.lat_p50_ms;
+      p90 = ss.lat_p90_ms;
+      p99 = ss.lat_p99_ms;
+      p999 = ss.lat_p999_ms;
+      lmax = ss.lat_max_ms;
+      expansions = ss.expansions;
+      admission_params = " max_inflight=" + std::to_string(ss.max_inflight) +
+                         " prefeed=" + std::to_string(ss.max_inflight - ss.workers) +
+                         " admissions=" + std::to_string(ss.admissions);
+    } else {
+      qv_search_stats st{};
+      const auto t0 = std::chrono::steady_clock::now();
+      if (qv_search_timed(eng, queries.data(), static_cast<int64_t>(nq), info.dim, &so, ids.data(), dists.data(),
+                          found.data(), lat.data(), &st) != QV_OK) {
+        std::cerr << qv_last_error() << std::endl;
+        qv_engine_destroy(eng);
+        return 1;
+      }
+      const double secs = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+      std::vector<double> l(lat.begin(), lat.end());
+      std::sort(l.begin(), l.end());
+      qps = secs > 0 ? nq / secs : 0.0;
+      avg = l.empty() ? 0.0 : std::accumulate(l.begin(), l.end(), 0.0) / l.size();
+      p50 = pct(l, 0.50);
+      p90 = pct(l, 0.90);
+      p99 = pct(l, 0.99);
+      p999 = pct(l, 0.999);
+      lmax = l.empty() ? 0.0 : l.back();
+      expansions = st.expansions;
+    }
     // run_report.hpp:96-140 layout
     std::ostringstream os;
     os << std::fixed;
     os << "========== Quiver Result ==========\n";
     os << "Query Params:\n  topk=" << a.topk << " ef_search=" << a.ef_search << " repeat=" << a.repeat
        << " data_type=" << a.data_type << "\n";
-    os << "Runtime Params:\n  num_blocks=" << st.grid << " pipe_width=" << a.pipe_width
-       << " queries_per_block=" << st.slots_per_block << " task_slots=" << st.grid * st.slots_per_block
-       << " io_slots=" << st.grid * st.slots_per_block * a.pipe_width << " page_store=" << a.page_store
-       << " engine=" << qv_version() << "\n\n";
-    os << "Performance:\n  QPS: " << std::setprecision(2) << (secs > 0 ? nq / secs : 0.0) << "\n";
-    os << "  QueryLatency(ms): avg=" << std::setprecision(3) << avg << " p50=" << pct(l, 0.50)
-       << " p90=" << pct(l, 0.90) << " p99=" << pct(l, 0.99) << " p99.9=" << pct(l, 0.999)
-       << " max=" << (l.empty() ? 0.0 : l.back()) << "\n";
+    os << "Runtime Params:\n  num_blocks=" << plan.grid << " pipe_width=" << a.pipe_width
+       << " queries_per_block=" << plan.slots_per_block << " task_slots=" << plan.grid * plan.slots_per_block
+       << " io_slots=" << plan.grid * plan.slots_per_block * a.pipe_width << " admission=" << a.admission
+       << admission_params << " page_store=" << a.page_store << " engine=" << qv_version() << "\n\n";
+    os << "Performance:\n  QPS: " << std::setprecision(2) << qps << "\n";
+    os << "  QueryLatency(ms): avg=" << std::setprecision(3) << avg << " p50=" << p50 << " p90=" << p90
+       << " p99=" << p99 << " p99.9=" << p999 << " max=" << lmax << "\n";
     os << "  SSD Avg Bandwidth: 0.00 GB/s\n  SSD Avg IOPS: 0\n";
     os << "===================================\n";
     std::printf("%s", os.str().c_str());
     std::cout << "[Quiver] Finish summary: policy=" << (policy == QV_EXIT_NONE ? "none" : "gpruning")
               << " avg_finish_step=" << std::fixed << std::setprecision(2)
-              << (nq ? static_cast<double>(st.expansions) / nq : 0.0) << " finished=" << nq << "/" << nq
+              << (nq ? static_cast<double>(expansions) / nq : 0.0) << " finished=" << nq << "/" << nq
               << std::defaultfloat << std::endl;
 
     if (!a.ground_truth_file.empty()) {  // search_setup.hpp:163-174

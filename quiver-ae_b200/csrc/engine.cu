@@ -15,6 +15,7 @@
 #include <cstring>
 #include <memory>
 #include <mutex>
+#include <numeric>
 #include <string>
 #include <vector>
 
@@ -100,6 +101,14 @@ struct qv_engine {
   unsigned long long* d_visited = nullptr;
   size_t visited_bytes = 0;
   uint32_t visited_next = 1;
+  // streaming admission: copy stream, per-worker completion counts (pinned,
+  // mapped), feed values the copy stream writes to the device (pinned ring),
+  // one event per ring slot
+  cudaStream_t h2d_stream = nullptr;
+  uint32_t* h_done = nullptr;
+  int32_t* h_feed = nullptr;
+  std::vector<cudaEvent_t> feed_ev;
+  int64_t cap_done = 0;
 
   ~qv_engine() {
     if (device >= 0) cudaSetDevice(device);
@@ -122,6 +131,11 @@ struct qv_engine {
     if (d_stripe_table) cudaFree(d_stripe_table);
     for (auto& e : ev)
       if (e) cudaEventDestroy(e);
+    for (auto& e : feed_ev)
+      if (e) cudaEventDestroy(e);
+    if (h_done) cudaFreeHost(h_done);
+    if (h_feed) cudaFreeHost(h_feed);
+    if (h2d_stream) cudaStreamDestroy(h2d_stream);
     if (stream) cudaStreamDestroy(stream);
   }
 };
@@ -328,6 +342,7 @@ void read_device_status(qv_engine* e) {
                    : info[0] == qvk::kErrHopCap        ? "a walk beyond its iteration bound"
                    : info[0] == qvk::kErrNav           ? "a nav graph id out of range or a nav walk beyond its bound"
                    : info[0] == qvk::kErrVisited       ? "a full visited-filter table"
+                   : info[0] == qvk::kErrFeed          ? "a query not admitted within the feed timeout"
                                                        : "an unknown device error";
   fail(QV_ERR_DEVICE, std::string("search kernel found ") + what + " (query " +
                           std::to_string(info[1]) + ", node/step " + std::to_string(info[2]) + ")");
@@ -790,6 +805,198 @@ int qv_search(qv_engine* e, const float* queries, int64_t nq, int64_t dim, const
 int qv_search_timed(qv_engine* e, const float* queries, int64_t nq, int64_t dim, const qv_search_opts* opts,
                     int32_t* ids, float* dists, int32_t* found, float* query_ms, qv_search_stats* stats) {
   return search_host(e, queries, nq, dim, opts, ids, dists, found, query_ms, stats);
+}
+
+void qv_stream_opts_default(qv_stream_opts* o) {
+  if (!o) return;
+  o->prefeed = -1;
+  o->admit_min_batch = 32;
+  o->feed_timeout_ms = 10000;
+  o->admit_limit = -1;
+}
+
+}  // extern "C"
+
+namespace {
+
+// Page-locks a caller's host array for the duration of a call; an array that
+// is already registered (or a platform that refuses) is used as it is.
+struct HostRegistration {
+  void* ptr = nullptr;
+  HostRegistration(const void* p, size_t bytes) {
+    if (!p || bytes == 0) return;
+    if (cudaHostRegister(const_cast<void*>(p), bytes, cudaHostRegisterDefault) == cudaSuccess)
+      ptr = const_cast<void*>(p);
+    else
+      cudaGetLastError();
+  }
+  ~HostRegistration() {
+    if (ptr) cudaHostUnregister(ptr);
+  }
+  HostRegistration(const HostRegistration&) = delete;
+  HostRegistration& operator=(const HostRegistration&) = delete;
+};
+
+void ensure_stream_buffers(qv_engine* e, int64_t workers, int64_t ring) {
+  if (!e->h2d_stream) CK(cudaStreamCreateWithFlags(&e->h2d_stream, cudaStreamNonBlocking));
+  if (workers > e->cap_done) {
+    if (e->h_done) CK(cudaFreeHost(e->h_done));
+    e->h_done = nullptr;
+    CK(cudaHostAlloc(&e->h_done, workers * sizeof(uint32_t), cudaHostAllocMapped));
+    e->cap_done = workers;
+  }
+  if (ring > static_cast<int64_t>(e->feed_ev.size())) {
+    if (e->h_feed) CK(cudaFreeHost(e->h_feed));
+    e->h_feed = nullptr;
+    CK(cudaHostAlloc(&e->h_feed, ring * sizeof(int32_t), cudaHostAllocDefault));
+    const size_t old = e->feed_ev.size();
+    e->feed_ev.resize(ring, nullptr);
+    for (size_t i = old; i < e->feed_ev.size(); ++i)
+      CK(cudaEventCreateWithFlags(&e->feed_ev[i], cudaEventDisableTiming));
+  }
+}
+
+}  // namespace
+
+extern "C" {
+
+int qv_search_stream(qv_engine* e, const float* queries, int64_t nq, int64_t dim, const qv_search_opts* opts,
+                     const qv_stream_opts* sopts, int32_t* ids, float* dists, int32_t* found,
+                     float* query_latency_ms, qv_stream_stats* stats) {
+  return guarded([&] {
+    if (!e || !opts || (nq > 0 && (!queries || !ids || !dists))) fail(QV_ERR_INVALID_ARG, "null argument");
+    if (nq < 0) fail(QV_ERR_INVALID_ARG, "nq must be non-negative");
+    if (nq > INT32_MAX / 2) fail(QV_ERR_INVALID_ARG, "nq above 2^30");
+    if (dim != e->L.dim)
+      fail(QV_ERR_INVALID_ARG, "Query dimension mismatch: queries have " + std::to_string(dim) +
+                                   " dims, but the index expects " + std::to_string(e->L.dim));
+    qv_stream_opts so;
+    qv_stream_opts_default(&so);
+    if (sopts) so = *sopts;
+    if (so.admit_min_batch < 1) fail(QV_ERR_INVALID_ARG, "admit_min_batch must be >= 1");
+    if (so.feed_timeout_ms < 1) fail(QV_ERR_INVALID_ARG, "feed_timeout_ms must be >= 1");
+    CK(cudaSetDevice(e->device));
+    const Plan pl = make_plan(e, *opts, std::max<int64_t>(nq, 1));
+    if (stats) std::memset(stats, 0, sizeof(*stats));
+    if (nq == 0) return;
+    const int64_t workers = pl.block ? pl.grid : static_cast<int64_t>(pl.grid) * pl.slots;
+    const int64_t prefeed = so.prefeed < 0 ? workers : so.prefeed;
+    const int64_t max_inflight = std::max<int64_t>(1, workers + prefeed);
+    const int64_t ring = std::max<int64_t>(64, 2 * max_inflight);
+    ensure_staging(e, nq, opts->topk);
+    ensure_stream_buffers(e, workers, ring);
+    HostRegistration reg(queries, static_cast<size_t>(nq) * dim * sizeof(float));
+    std::memset(e->h_done, 0, workers * sizeof(uint32_t));
+    uint32_t* d_done = nullptr;
+    CK(cudaHostGetDevicePointer(reinterpret_cast<void**>(&d_done), e->h_done, 0));
+    auto p = make_params(e, pl, *opts, e->d_q, nq, e->d_ids, e->d_dists, e->d_found,
+                         stats ? e->d_steps : nullptr, nullptr);
+    p.feed = e->d_scratch + 6;
+    p.done_slots = d_done;
+    p.feed_timeout_ns = static_cast<int64_t>(so.feed_timeout_ms) * 1000000;
+    cudaStream_t ks = e->stream, hs = e->h2d_stream;
+    prepare_visited(e, pl, *opts, nq, p, ks);
+    CK(cudaStreamSynchronize(ks));
+
+    using clock = std::chrono::steady_clock;
+    const auto t0 = clock::now();
+    auto now_ms = [&] { return std::chrono::duration<double, std::milli>(clock::now() - t0).count(); };
+    const int64_t limit = so.admit_limit < 0 ? nq : std::min<int64_t>(nq, so.admit_limit);
+    std::vector<double> start(nq, 0.0), lat(nq, 0.0);
+    // First range before the launch (search.cu:853-890): copied and made visible synchronously.
+    const int64_t initial = std::min(max_inflight, limit);
+    e->h_feed[0] = static_cast<int32_t>(initial);
+    CK(cudaMemsetAsync(e->d_scratch, 0, 8 * sizeof(int32_t), hs));
+    if (initial > 0) CK(cudaMemcpyAsync(e->d_q, queries, initial * dim * 4, cudaMemcpyHostToDevice, hs));
+    CK(cudaMemcpyAsync(e->d_scratch + 6, e->h_feed, sizeof(int32_t), cudaMemcpyHostToDevice, hs));
+    CK(cudaStreamSynchronize(hs));
+    int64_t admissions = 1;
+    pl.launch(p, pl.grid, pl.threads, pl.smem, ks);
+    CK(cudaGetLastError());
+
+    // Admission loop (search.cu:983-1051): retire finished copies, charge new
+    // completions, admit the next range when flow control allows.
+    const volatile uint32_t* done_slots = e->h_done;
+    int64_t last_done = 0, next = initial, head = 0, pending = 0;
+    uint64_t polls = 0;
+    while (last_done < nq) {
+      while (pending > 0) {
+        const cudaError_t q = cudaEventQuery(e->feed_ev[head]);
+        if (q == cudaErrorNotReady) break;
+        CK(q);
+        head = (head + 1) % ring;
+        --pending;
+      }
+      int64_t done = 0;
+      for (int64_t w = 0; w < workers; ++w) done += done_slots[w];
+      if (done > last_done) {
+        const double t = now_ms();
+        for (int64_t i = last_done; i < std::min(done, nq); ++i) lat[i] = t - start[i];
+        last_done = std::min(done, nq);
+        if (last_done >= nq) break;
+      }
+      const int64_t target = std::min(limit, last_done + max_inflight);
+      const int64_t gap = target - next;
+      if (gap > 0 && pending < ring && (gap >= so.admit_min_batch || target == limit || pending == 0)) {
+        const double t = now_ms();
+        const int64_t slot = (head + pending) % ring;
+        e->h_feed[slot] = static_cast<int32_t>(target);
+        CK(cudaMemcpyAsync(e->d_q + next * dim, queries + next * dim, gap * dim * 4, cudaMemcpyHostToDevice, hs));
+        CK(cudaMemcpyAsync(e->d_scratch + 6, e->h_feed + slot, sizeof(int32_t), cudaMemcpyHostToDevice, hs));
+        CK(cudaEventRecord(e->feed_ev[slot], hs));
+        for (int64_t i = next; i < target; ++i) start[i] = t;
+        next = target;
+        ++pending;
+        ++admissions;
+      }
+      if ((++polls & 255) == 0) {
+        // The kernel ended (or failed) with queries still outstanding: a worker gave up on its feed.
+        const cudaError_t q = cudaStreamQuery(ks);
+        if (q == cudaSuccess) {
+          int64_t d2 = 0;
+          for (int64_t w = 0; w < workers; ++w) d2 += done_slots[w];
+          if (d2 < nq) {
+            CK(cudaStreamSynchronize(hs));
+            read_device_status(e);
+            fail(QV_ERR_DEVICE, "streaming search ended with " + std::to_string(d2) + " of " +
+                                    std::to_string(nq) + " queries completed");
+          }
+        } else if (q != cudaErrorNotReady) {
+          CK(q);
+        }
+      }
+    }
+    const double search_ms = now_ms();
+    CK(cudaStreamSynchronize(ks));
+    CK(cudaStreamSynchronize(hs));
+    read_device_status(e);
+    CK(cudaMemcpyAsync(ids, e->d_ids, nq * opts->topk * 4, cudaMemcpyDeviceToHost, ks));
+    CK(cudaMemcpyAsync(dists, e->d_dists, nq * opts->topk * 4, cudaMemcpyDeviceToHost, ks));
+    if (found) CK(cudaMemcpyAsync(found, e->d_found, nq * 4, cudaMemcpyDeviceToHost, ks));
+    CK(cudaStreamSynchronize(ks));
+    if (query_latency_ms)
+      for (int64_t i = 0; i < nq; ++i) query_latency_ms[i] = static_cast<float>(lat[i]);
+    if (stats) {
+      // Percentiles as the reference reports them (search.cu:1140-1152).
+      std::vector<double> sorted(lat);
+      std::sort(sorted.begin(), sorted.end());
+      const size_t n = sorted.size();
+      stats->search_ms = search_ms;
+      stats->qps = nq / (search_ms / 1000.0);
+      stats->lat_avg_ms = std::accumulate(sorted.begin(), sorted.end(), 0.0) / n;
+      stats->lat_p50_ms = sorted[n * 50 / 100];
+      stats->lat_p90_ms = sorted[n * 90 / 100];
+      stats->lat_p99_ms = sorted[n * 99 / 100];
+      stats->lat_p999_ms = sorted[static_cast<size_t>(n * 0.999)];
+      stats->lat_max_ms = sorted[n - 1];
+      stats->admissions = admissions;
+      stats->workers = static_cast<int32_t>(workers);
+      stats->max_inflight = static_cast<int32_t>(max_inflight);
+      std::vector<int32_t> steps(nq);
+      CK(cudaMemcpy(steps.data(), e->d_steps, nq * 4, cudaMemcpyDeviceToHost));
+      for (int64_t i = 0; i < nq; ++i) stats->expansions += steps[i];
+    }
+  });
 }
 
 int qv_search_device(qv_engine* e, const float* d_queries, int64_t nq, const qv_search_opts* opts,

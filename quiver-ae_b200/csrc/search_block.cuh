@@ -1124,13 +1124,19 @@ template <typename T, int MC, int RP>
 __global__ void __launch_bounds__(kBlock, 5) search_block_kernel(const SearchParams p) {
   extern __shared__ __align__(16) uint8_t smem[];
   const BSlot s = make_bslot(smem, p.lay);
+  uint32_t done = 0;
   while (true) {
-    if (threadIdx.x == 0) s.misc[kMiscQid] = atomicAdd(p.work_counter, 1);
+    if (threadIdx.x == 0) {
+      int q = atomicAdd(p.work_counter, 1);
+      if (q < p.nq && !wait_fed(p, q)) q = INT32_MAX;
+      s.misc[kMiscQid] = q;
+    }
     __syncthreads();
     const int qid = s.misc[kMiscQid];
     __syncthreads();
     if (qid >= p.nq) break;
     run_query_block<T, MC, RP>(p, s, qid);
+    if (threadIdx.x == 0) mark_done(p, blockIdx.x, ++done);
   }
 }
 

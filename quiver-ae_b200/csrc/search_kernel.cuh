@@ -40,6 +40,7 @@ enum DeviceError : int32_t {
   kErrHopCap = 3,         // walk exceeded its iteration bound
   kErrNav = 4,            // nav graph: id out of range or entry search over its bound
   kErrVisited = 5,        // visited-filter table full
+  kErrFeed = 6,           // streaming admission: a query was not fed within the feed timeout
 };
 
 // Byte offsets of one query slot's arrays inside the CTA's shared memory.
@@ -101,6 +102,15 @@ struct SearchParams {
   unsigned long long* visited;
   int32_t visited_cap;           // power of two
   uint32_t visited_tag0;         // tag of query qid = visited_tag0 + qid
+  // streaming admission (feed == nullptr: every query is in `queries` at launch).
+  // Queries [0, *feed) have been copied in; the host advances *feed in stream
+  // order after each copy.  A worker (CTA of the block kernel, warp of the
+  // warp kernel) that binds query qid waits until *feed > qid, at most
+  // feed_timeout_ns, and after each query stores its running completion count
+  // to done_slots[worker] (host-mapped memory the host polls).
+  const int32_t* feed;
+  uint32_t* done_slots;
+  int64_t feed_timeout_ns;
   SlotLayout lay;
 };
 
@@ -755,6 +765,39 @@ __device__ __forceinline__ int64_t globaltimer_ns() {
   return static_cast<int64_t>(t);
 }
 
+__device__ __forceinline__ int32_t load_feed(const int32_t* f) {
+  int32_t v;
+  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+  return v;
+}
+
+// Streaming admission: true once query qid has been fed.  The wait is bounded
+// by p.feed_timeout_ns of the global timer (and by an iteration count, each
+// iteration sleeping at least 64 ns); when it runs out the worker reports
+// kErrFeed and the caller stops.
+static __device__ bool wait_fed(const SearchParams& p, int64_t qid) {
+  if (!p.feed || load_feed(p.feed) > qid) return true;
+  const int64_t t0 = globaltimer_ns();
+  const int64_t max_iters = p.feed_timeout_ns / 64 + 1024;
+  unsigned sleep_ns = 64;
+  for (int64_t it = 0; it < max_iters; ++it) {
+    __nanosleep(sleep_ns);
+    if (load_feed(p.feed) > qid) return true;
+    if (globaltimer_ns() - t0 > p.feed_timeout_ns) break;
+    sleep_ns = sleep_ns < 2048 ? 2 * sleep_ns : 2048;
+  }
+  report_error(p, kErrFeed, qid, load_feed(p.feed), 0);
+  return false;
+}
+
+// Streaming admission: publish a worker's running completion count.
+__device__ __forceinline__ void mark_done(const SearchParams& p, int worker, uint32_t count) {
+  if (p.done_slots) {
+    volatile uint32_t* slot = p.done_slots + worker;
+    *slot = count;
+  }
+}
+
 template <typename T, int MC, int SMAX>
 __device__ void run_query(const SearchParams& p, const Slot& s, int64_t qid, int lane) {
   if (p.out_time && lane == 0) p.out_time[2 * qid] = globaltimer_ns();
@@ -833,12 +876,18 @@ __global__ void __launch_bounds__(256) search_kernel(const SearchParams p) {
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   const Slot s = make_slot(smem + static_cast<size_t>(warp) * p.lay.bytes, p.lay);
+  const int worker = blockIdx.x * (blockDim.x >> 5) + warp;
+  uint32_t done = 0;
   while (true) {
     int qid = 0;
-    if (lane == 0) qid = atomicAdd(p.work_counter, 1);
+    if (lane == 0) {
+      qid = atomicAdd(p.work_counter, 1);
+      if (qid < p.nq && !wait_fed(p, qid)) qid = INT32_MAX;
+    }
     qid = __shfl_sync(kFull, qid, 0);
     if (qid >= p.nq) break;
     run_query<T, MC, SMAX>(p, s, qid, lane);
+    if (lane == 0) mark_done(p, worker, ++done);
   }
 }
 

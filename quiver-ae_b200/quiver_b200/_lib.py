@@ -67,6 +67,20 @@ class SearchStats(C.Structure):
     ]
 
 
+class StreamOpts(C.Structure):
+    _fields_ = [("prefeed", C.c_int32), ("admit_min_batch", C.c_int32), ("feed_timeout_ms", C.c_int32),
+                ("admit_limit", C.c_int32)]
+
+
+class StreamStats(C.Structure):
+    _fields_ = [
+        ("search_ms", C.c_double), ("qps", C.c_double), ("lat_avg_ms", C.c_double), ("lat_p50_ms", C.c_double),
+        ("lat_p90_ms", C.c_double), ("lat_p99_ms", C.c_double), ("lat_p999_ms", C.c_double),
+        ("lat_max_ms", C.c_double), ("admissions", C.c_int64), ("workers", C.c_int32), ("max_inflight", C.c_int32),
+        ("expansions", C.c_int64),
+    ]
+
+
 # Every symbol include/quiver_b200.h declares, with (restype, argtypes).
 ENGINE_SYMBOLS = {
     "qv_version": (C.c_char_p, []),
@@ -85,6 +99,10 @@ ENGINE_SYMBOLS = {
                             C.c_void_p, C.c_void_p, C.c_void_p, C.POINTER(SearchStats)]),
     "qv_search_timed": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int64, C.c_int64, C.POINTER(SearchOpts),
                                   C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.POINTER(SearchStats)]),
+    "qv_stream_opts_default": (None, [C.POINTER(StreamOpts)]),
+    "qv_search_stream": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int64, C.c_int64, C.POINTER(SearchOpts),
+                                   C.POINTER(StreamOpts), C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                                   C.POINTER(StreamStats)]),
     "qv_search_device": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int64, C.POINTER(SearchOpts), C.c_void_p,
                                    C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
     "qv_search_noalloc": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int64, C.c_int64, C.POINTER(SearchOpts),

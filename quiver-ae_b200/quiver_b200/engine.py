@@ -177,6 +177,28 @@ class Engine:
                                          C.c_void_p(found.ctypes.data), C.c_void_p(ms.ctypes.data), C.byref(st)))
         return ids, dists, found, ms, st
 
+    def search_stream(self, queries: np.ndarray, params: SearchParams | None = None, *, prefeed: int = -1,
+                      admit_min_batch: int = 32, feed_timeout_ms: int = 10000, admit_limit: int = -1):
+        """qv_search_stream: one persistent launch, queries admitted by the host
+        as completions allow (the reference's streaming loop).  Returns (ids,
+        dists, found, latency_ms, stats) with the reference's QueryLatency
+        definition (admission to observed completion, in completion order)."""
+        params = params or SearchParams()
+        q = np.ascontiguousarray(queries, dtype=np.float32)
+        nq, dim = q.shape
+        ids = np.empty((nq, params.topk), dtype=np.int32)
+        dists = np.empty((nq, params.topk), dtype=np.float32)
+        found = np.empty(nq, dtype=np.int32)
+        lat = np.empty(nq, dtype=np.float32)
+        so = _lib.StreamOpts(prefeed, admit_min_batch, feed_timeout_ms, admit_limit)
+        st = _lib.StreamStats()
+        o = params.to_c()
+        _check(self._lib.qv_search_stream(self._h, C.c_void_p(q.ctypes.data), nq, dim, C.byref(o), C.byref(so),
+                                          C.c_void_p(ids.ctypes.data), C.c_void_p(dists.ctypes.data),
+                                          C.c_void_p(found.ctypes.data), C.c_void_p(lat.ctypes.data),
+                                          C.byref(st)))
+        return ids, dists, found, lat, st
+
     def search_noalloc(self, queries: np.ndarray, params: SearchParams | None = None):
         """qv_search_noalloc: the same search with no device allocation on the call
         path (its scratch is a fixed 4 MiB device array); returns (ids, dists, found)."""
