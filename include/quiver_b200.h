@@ -290,6 +290,16 @@ int qv_exact_l2_device(qv_engine* engine, const float* d_q2, const int32_t* d_qu
  * multiple of 4 and d_luts 16-byte aligned.  kernel picks the implementation:
  * QV_ADC_PIPE (M == 32, 16-byte aligned codes; for thousands of codes per
  * query), QV_ADC_THREAD (any M), or QV_ADC_AUTO.  Asynchronous on stream. */
+/* Vamana graph built on the GPU: the construction of qvb_vamana
+ * (include/quiver_b200_build.h) step for step -- same medoid, insertion
+ * order, batches, distances and prune -- so the graph, degrees and medoid
+ * equal the host builder's.  base is a HOST array [n x dim] of dtype
+ * (QV_UINT8, QV_INT8, QV_FLOAT); R <= 128, L <= 256, dim <= 1024; graph
+ * [n x R] (-1 padded), degree [n] and medoid are host outputs. */
+int qv_vamana_gpu(const void* base, int64_t n, int64_t dim, int32_t dtype, int32_t R,
+                  int32_t L, float alpha, int32_t passes, uint64_t seed, int32_t device,
+                  int32_t* graph, int32_t* degree, int64_t* medoid);
+
 #define QV_ADC_AUTO 0
 #define QV_ADC_THREAD 1
 #define QV_ADC_PIPE 2

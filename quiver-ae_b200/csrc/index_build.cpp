@@ -19,6 +19,7 @@
 
 #include "quiver_b200.h"
 #include "quiver_b200_build.h"
+#include "vamana_common.h"
 
 namespace {
 
@@ -26,14 +27,7 @@ thread_local std::string g_err;
 
 // ------------------------------------------------------------ generator --
 
-inline uint64_t mix64(uint64_t z) {  // splitmix64 finaliser
-  z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ULL;
-  z = (z ^ (z >> 27)) * 0x94d049bb133111ebULL;
-  return z ^ (z >> 31);
-}
-inline uint64_t hash3(uint64_t seed, uint64_t stream, uint64_t idx) {
-  return mix64(mix64(seed * 0x9e3779b97f4a7c15ULL + stream) ^ (idx * 0xd1b54a32d192ed03ULL + 0x632be59bd9b4e019ULL));
-}
+using qv_vamana::hash3;
 inline double u01(uint64_t h) { return static_cast<double>(h >> 11) * (1.0 / 9007199254740992.0); }
 // Irwin-Hall(12) - 6: mean 0, variance 1.
 inline double gauss(uint64_t seed, uint64_t stream, uint64_t idx) {
@@ -193,39 +187,18 @@ struct Vamana {
   }
 
   void run(float alpha_final, int32_t passes, uint64_t seed, int nthreads) {
-    // medoid: the point nearest the mean
-    std::vector<double> mean(static_cast<size_t>(dim), 0.0);
-    for (int64_t i = 0; i < n; ++i)
-      for (int64_t d = 0; d < dim; ++d) mean[d] += static_cast<double>(vec(i)[d]);
-    for (auto& m : mean) m /= static_cast<double>(n);
-    {
-      double best = 1e300;
-      for (int64_t i = 0; i < n; ++i) {
-        double s = 0.0;
-        for (int64_t d = 0; d < dim; ++d) {
-          const double t = static_cast<double>(vec(i)[d]) - mean[d];
-          s += t * t;
-        }
-        if (s < best) { best = s; medoid = i; }
-      }
-    }
+    medoid = qv_vamana::medoid(data, n, dim);
     std::fill(degree.begin(), degree.end(), 0);
     std::fill(graph.begin(), graph.end(), -1);
-    // insertion order: seeded Fisher-Yates
-    std::vector<int64_t> perm(static_cast<size_t>(n));
-    std::iota(perm.begin(), perm.end(), 0);
-    for (int64_t i = n - 1; i > 0; --i) {
-      const int64_t j = static_cast<int64_t>(hash3(seed, 77, static_cast<uint64_t>(i)) % static_cast<uint64_t>(i + 1));
-      std::swap(perm[i], perm[j]);
-    }
-    const int64_t max_batch = std::max<int64_t>(1, std::min<int64_t>(n / 50, 20000));
+    const std::vector<int64_t> perm = qv_vamana::insertion_order(seed, n);
+    const int64_t max_batch = qv_vamana::max_batch(n);
     std::vector<Scratch> scratch(static_cast<size_t>(nthreads));
     for (auto& s : scratch) s.seen.assign(static_cast<size_t>(n), 0u);
     std::vector<std::vector<int32_t>> newlist;
     for (int32_t pass = 0; pass < passes; ++pass) {
-      const float alpha = (passes > 1 && pass == 0) ? 1.0f : alpha_final;
+      const float alpha = qv_vamana::pass_alpha(pass, passes, alpha_final);
       int64_t start = 0;
-      int64_t bsize = pass == 0 ? 1 : max_batch;
+      int64_t bsize = qv_vamana::first_batch(pass, n);
       while (start < n) {
         const int64_t end = std::min(n, start + bsize);
         const int64_t cnt = end - start;

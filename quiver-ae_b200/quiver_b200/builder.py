@@ -100,15 +100,35 @@ def pq_encode(base: np.ndarray, pivots: np.ndarray, centroid: np.ndarray, chunk_
     return codes
 
 
+def vamana_gpu(base: np.ndarray, R: int, L: int, alpha: float, passes: int = 2, seed: int = 0,
+               device: int = 0) -> tuple[np.ndarray, np.ndarray, int]:
+    """The same construction as ``vamana`` on a GPU (qv_vamana_gpu): equal graph, degrees and medoid."""
+    from . import engine
+    base = np.ascontiguousarray(base)
+    n, dim = base.shape
+    dtype = {np.dtype(np.uint8): _lib.QV_UINT8, np.dtype(np.int8): _lib.QV_INT8,
+             np.dtype(np.float32): _lib.QV_FLOAT}[base.dtype]
+    graph = np.empty((n, R), dtype=np.int32)
+    degree = np.empty(n, dtype=np.int32)
+    medoid = C.c_int64(0)
+    engine._check(_lib.engine_lib().qv_vamana_gpu(_ptr(base), n, dim, dtype, R, L, alpha, passes, seed, device,
+                                                  _ptr(graph), _ptr(degree), C.byref(medoid)))
+    return graph, degree, int(medoid.value)
+
+
 def build_index(index_dir: str | Path, base: np.ndarray, *, R: int = 64, L: int = 100, alpha: float = 1.2,
                 M: int = 32, passes: int = 2, pq_sample: int = 100_000, pq_iters: int = 12, seed: int = 0,
-                prefix: str = "ann", nthreads: int = 0) -> BuiltIndex:
-    """Write ``<prefix>_disk.index``, ``<prefix>_pq_pivots.bin`` and ``<prefix>_pq_compressed.bin``."""
+                prefix: str = "ann", nthreads: int = 0, graph_device: int | None = None) -> BuiltIndex:
+    """Write ``<prefix>_disk.index``, ``<prefix>_pq_pivots.bin`` and ``<prefix>_pq_compressed.bin``.
+    graph_device: build the graph on that GPU (the same graph as the host builder's)."""
     index_dir = Path(index_dir)
     index_dir.mkdir(parents=True, exist_ok=True)
     base = np.ascontiguousarray(base)
     data_type = {np.dtype(np.uint8): "uint8", np.dtype(np.int8): "int8", np.dtype(np.float32): "float"}[base.dtype]
-    graph, degree, medoid = vamana(base, R, L, alpha, passes, seed, nthreads)
+    if graph_device is None:
+        graph, degree, medoid = vamana(base, R, L, alpha, passes, seed, nthreads)
+    else:
+        graph, degree, medoid = vamana_gpu(base, R, L, alpha, passes, seed, graph_device)
     layout = formats.write_disk_index(index_dir / f"{prefix}_disk.index", base, graph, degree, medoid, R)
     pivots, centroid, offs = pq_train(base, M, pq_sample, pq_iters, seed, nthreads)
     codes = pq_encode(base, pivots, centroid, offs, nthreads)
