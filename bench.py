@@ -143,7 +143,13 @@ def reference_arm(args, rank: int, world: int) -> int:
     from oracle import pyoracle
     from quiver_b200 import workloads
     w = workloads.CONFIGS[args.config]
-    d = workloads.prepare(w, log=log)
+    # the index is the search's input: build it on the GPU when there is one (the same files as a host build)
+    try:
+        import torch
+        build_dev = 0 if torch.cuda.is_available() else None
+    except ImportError:
+        build_dev = None
+    d = workloads.prepare(w, log=log, device=build_dev)
     ix = pyoracle.load_index(d, w.data_type)
     nav = pyoracle.load_nav(workloads.prepare_nav(w, log=log), w.data_type) if args.nav else None
     qc = workloads.queries(w, rows=CALIB_QUERIES).astype(np.float32)
@@ -330,7 +336,7 @@ def main() -> int:
 
     w = workloads.CONFIGS[args.config]
     if rank == 0:
-        workloads.prepare(w, log=log)
+        workloads.prepare(w, log=log, device=local)
         if args.nav:
             workloads.prepare_nav(w, log=log)
     barrier()
@@ -468,6 +474,7 @@ def main() -> int:
                        "l2": f"inputs larger than L2: page store {info.num_pages * 4096 / 1e6:.0f} MB + codes "
                              f"{info.num_points * info.num_chunks / 1e6:.0f} MB vs 126 MB L2, no flush",
                        "parallelism": f"query shards x{world}, index replicated",
+                       "index_build": workloads.build_info(w),
                        "page_store": f"striped over GPUs {stripes} (peer loads)" if stripes else "HBM of the search GPU"},
             "recall_at_10": recall,
             "p50_ms": streaming["p50_ms"] if streaming else None,

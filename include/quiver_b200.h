@@ -300,6 +300,15 @@ int qv_vamana_gpu(const void* base, int64_t n, int64_t dim, int32_t dtype, int32
                   int32_t L, float alpha, int32_t passes, uint64_t seed, int32_t device,
                   int32_t* graph, int32_t* degree, int64_t* medoid);
 
+/* The seeded Gaussian-mixture generator of qvb_synth_mixture and the PQ
+ * encoder of qvb_pq_encode (include/quiver_b200_build.h) on the GPU, bit for
+ * bit.  Host buffers in and out; `device` is the CUDA device used. */
+int qv_synth_mixture_gpu(uint64_t seed, int32_t stream, int64_t row0, int64_t n, int64_t dim,
+                         int64_t n_centers, double sigma, int32_t dtype, void* out, int32_t device);
+int qv_pq_encode_gpu(const void* base, int64_t n, int64_t dim, int32_t dtype, int32_t M,
+                     const float* pivots, const float* centroid, const int32_t* chunk_offsets,
+                     int32_t device, uint8_t* codes);
+
 #define QV_ADC_AUTO 0
 #define QV_ADC_THREAD 1
 #define QV_ADC_PIPE 2

@@ -19,6 +19,7 @@
 
 #include "quiver_b200.h"
 #include "quiver_b200_build.h"
+#include "synth_common.h"
 #include "vamana_common.h"
 
 namespace {
@@ -28,34 +29,10 @@ thread_local std::string g_err;
 // ------------------------------------------------------------ generator --
 
 using qv_vamana::hash3;
-inline double u01(uint64_t h) { return static_cast<double>(h >> 11) * (1.0 / 9007199254740992.0); }
-// Irwin-Hall(12) - 6: mean 0, variance 1.
-inline double gauss(uint64_t seed, uint64_t stream, uint64_t idx) {
-  double s = 0.0;
-  for (int t = 0; t < 12; ++t) s = s + u01(hash3(seed, stream, idx * 12 + t));
-  return s - 6.0;
-}
-
-constexpr uint64_t kCenterStream = 1000, kAssignStream = 2000, kNoiseStream = 3000;
-
-std::vector<double> mixture_centers(uint64_t seed, int64_t k, int64_t dim, int32_t dtype) {
-  std::vector<double> c(static_cast<size_t>(k * dim));
-  for (int64_t i = 0; i < k; ++i) {
-    double* row = c.data() + i * dim;
-    if (dtype == QV_FLOAT) {
-      double nrm = 0.0;
-      for (int64_t d = 0; d < dim; ++d) {
-        row[d] = gauss(seed, kCenterStream, static_cast<uint64_t>(i * dim + d));
-        nrm = nrm + row[d] * row[d];
-      }
-      nrm = std::sqrt(nrm);
-      for (int64_t d = 0; d < dim; ++d) row[d] = row[d] / nrm;
-    } else {
-      for (int64_t d = 0; d < dim; ++d) row[d] = u01(hash3(seed, kCenterStream, i * dim + d)) * 255.0;
-    }
-  }
-  return c;
-}
+using qv_synth::gauss;
+using qv_synth::mixture_centers;
+using qv_synth::kAssignStream;
+using qv_synth::kNoiseStream;
 
 // ------------------------------------------------------------ distances --
 

@@ -15,16 +15,11 @@
 #include <numeric>
 #include <vector>
 
+#include "synth_common.h"
+
 namespace qv_vamana {
 
-inline uint64_t mix64(uint64_t z) {  // splitmix64 finaliser
-  z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ULL;
-  z = (z ^ (z >> 27)) * 0x94d049bb133111ebULL;
-  return z ^ (z >> 31);
-}
-inline uint64_t hash3(uint64_t seed, uint64_t stream, uint64_t idx) {
-  return mix64(mix64(seed * 0x9e3779b97f4a7c15ULL + stream) ^ (idx * 0xd1b54a32d192ed03ULL + 0x632be59bd9b4e019ULL));
-}
+using qv_synth::hash3;
 
 // The point nearest the mean (sums in double, in index order; first minimum).
 template <typename T>
@@ -60,7 +55,9 @@ inline std::vector<int64_t> insertion_order(uint64_t seed, int64_t n) {
   return perm;
 }
 
-inline int64_t max_batch(int64_t n) { return std::max<int64_t>(1, std::min<int64_t>(n / 50, 20000)); }
+// Batches grow to 2 % of n, at most 2^21 points (for n <= 1M that is at
+// most 20,000 points).
+inline int64_t max_batch(int64_t n) { return std::max<int64_t>(1, std::min<int64_t>(n / 50, int64_t(1) << 21)); }
 
 inline float pass_alpha(int32_t pass, int32_t passes, float alpha_final) {
   return (passes > 1 && pass == 0) ? 1.0f : alpha_final;

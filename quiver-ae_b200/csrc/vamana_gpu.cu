@@ -41,7 +41,7 @@ constexpr int kMaxL = 256;
 constexpr int kExpCap = 2048;                // expansions recorded per search
 constexpr int kPoolCap = kExpCap + kMaxR;    // expanded + current out-list
 constexpr int kSeenCap = 32768;              // hash-set entries per search (power of 2)
-constexpr int kChunk = 8192;                 // searches per launch (bounds the scratch)
+constexpr int kChunk = 32768;                // searches per launch (bounds the scratch)
 constexpr unsigned long long kNoKey = ~0ull;
 
 enum BuildError : int32_t { kBuildOk = 0, kErrExpansions = 1, kErrSeen = 2 };
@@ -409,42 +409,47 @@ __global__ void install_kernel(const VArgs a, int64_t first, int64_t cnt, unsign
 struct RevArgs {
   const unsigned long long* keys;
   int64_t total;
-  int32_t* heads;       // group start indices
-  int32_t* nheads;
-  unsigned long long* alloc;  // bump pointer into the pools
-  float* pd;
+  const int32_t* heads;  // group start indices, ascending
+  int32_t* nheads;       // [0] groups, [1] valid keys, [2] longest group
+  float* pd;             // per-warp pools of 2 (R + longest group) entries
   int32_t* pi;
-  int64_t pool_cap;
+  uint32_t* bits;        // per-warp prune flags, bits_per_warp words
+  int64_t pool_per_warp;
+  int64_t bits_per_warp;
 };
 
-__global__ void heads_kernel(RevArgs r) {
+// Group starts (unordered) and the number of valid keys.
+__global__ void heads_kernel(const unsigned long long* keys, int64_t total, int32_t* heads, int32_t* nheads) {
   const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (i >= r.total) return;
-  const unsigned long long k = r.keys[i];
+  if (i >= total) return;
+  const unsigned long long k = keys[i];
   if (k == kNoKey) return;
-  if (i == 0 || (r.keys[i - 1] >> 32) != (k >> 32)) r.heads[atomicAdd(r.nheads, 1)] = static_cast<int32_t>(i);
+  if (i == 0 || (keys[i - 1] >> 32) != (k >> 32)) heads[atomicAdd(nheads, 1)] = static_cast<int32_t>(i);
+  if (i + 1 == total || keys[i + 1] == kNoKey) nheads[1] = static_cast<int32_t>(i + 1);
+}
+
+// Longest group, from the sorted starts.
+__global__ void longest_kernel(const int32_t* heads, int32_t* nheads) {
+  const int g = blockIdx.x * blockDim.x + threadIdx.x;
+  const int nh = nheads[0];
+  if (g >= nh) return;
+  const int end = g + 1 < nh ? heads[g + 1] : nheads[1];
+  atomicMax(nheads + 2, end - heads[g]);
 }
 
 template <typename T>
 __global__ void __launch_bounds__(kWarps * 32) reverse_kernel(const VArgs a, RevArgs r, float alpha) {
-  extern __shared__ __align__(16) uint8_t smem[];
   const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
-  uint32_t* pruned = reinterpret_cast<uint32_t*>(smem) + wib * ((kPoolCap + 31) / 32);
-  const int nh = *r.nheads;
+  const int nh = r.nheads[0];
   const T* data = static_cast<const T*>(a.data);
-  for (int g = blockIdx.x * kWarps + wib; g < nh; g += gridDim.x * kWarps) {
+  const int64_t wid = static_cast<int64_t>(blockIdx.x) * kWarps + wib;
+  float* wpd = r.pd + wid * r.pool_per_warp;
+  int32_t* wpi = r.pi + wid * r.pool_per_warp;
+  uint32_t* pruned = r.bits + wid * r.bits_per_warp;
+  for (int g = static_cast<int>(wid); g < nh; g += gridDim.x * kWarps) {
     const int64_t h = r.heads[g];
     const int32_t j = static_cast<int32_t>(r.keys[h] >> 32);
-    int64_t e = h;
-    for (int64_t base = h;; base += 32) {
-      const int64_t k = base + lane;
-      const bool in = k < r.total && r.keys[k] != kNoKey && static_cast<int32_t>(r.keys[k] >> 32) == j;
-      const uint32_t m = __ballot_sync(0xffffffffu, !in);
-      if (m) {
-        e = base + __ffs(m) - 1;
-        break;
-      }
-    }
+    const int64_t e = g + 1 < nh ? r.heads[g + 1] : r.nheads[1];
     int32_t* nb = a.graph + static_cast<int64_t>(j) * a.R;
     const int deg = a.degree[j];
     // the p's of the group that are new to j, in ascending order
@@ -478,17 +483,10 @@ __global__ void __launch_bounds__(kWarps * 32) reverse_kernel(const VArgs a, Rev
       if (lane == 0) a.degree[j] = deg + nadd;
       continue;
     }
-    // overflow: re-prune old list + new p's
+    // overflow: re-prune old list + new p's (P <= R + longest group: the pool fits)
     const int P = deg + nadd;
-    unsigned long long off = 0;
-    if (lane == 0) off = atomicAdd(r.alloc, 2ull * P);
-    off = __shfl_sync(0xffffffffu, off, 0);
-    if (off + 2ull * P > static_cast<unsigned long long>(r.pool_cap)) {
-      if (lane == 0) set_error(a.err, kErrSeen + 1, j);
-      continue;
-    }
-    float* pd = r.pd + off;
-    int32_t* pi = r.pi + off;
+    float* pd = wpd;
+    int32_t* pi = wpi;
     const T* vj = data + static_cast<int64_t>(j) * a.dim;
     for (int t = lane; t < deg; t += 32) {
       pd[t] = VDist<T>::l2(vj, data + static_cast<int64_t>(nb[t]) * a.dim, a.dim);
@@ -529,6 +527,9 @@ int run_vamana(const T* h_data, int64_t n, int32_t dim, int32_t R, int32_t L, fl
     return e == cudaSuccess;
   };
   const int64_t medoid = qv_vamana::medoid(h_data, n, dim);
+  int dev = 0, num_sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, dev);
   const std::vector<int64_t> perm = qv_vamana::insertion_order(seed, n);
   const int64_t max_batch = qv_vamana::max_batch(n);
   VArgs a{};
@@ -554,24 +555,30 @@ int run_vamana(const T* h_data, int64_t n, int32_t dim, int32_t R, int32_t L, fl
   int64_t* d_perm = static_cast<int64_t*>(alloc(static_cast<size_t>(n) * 8));
   a.newlist = static_cast<int32_t*>(alloc(static_cast<size_t>(max_batch) * R * 4));
   a.newdeg = static_cast<int32_t*>(alloc(static_cast<size_t>(max_batch) * 4));
-  a.seen = static_cast<unsigned long long*>(alloc(static_cast<size_t>(kChunk) * kSeenCap * 8));
-  a.pool_d = static_cast<float*>(alloc(static_cast<size_t>(kChunk) * 2 * kPoolCap * 4));
-  a.pool_i = static_cast<int32_t*>(alloc(static_cast<size_t>(kChunk) * 2 * kPoolCap * 4));
+  const int64_t chunk = std::min<int64_t>(kChunk, max_batch);  // searches per launch
+  a.seen = static_cast<unsigned long long*>(alloc(static_cast<size_t>(chunk) * kSeenCap * 8));
+  a.pool_d = static_cast<float*>(alloc(static_cast<size_t>(chunk) * 2 * kPoolCap * 4));
+  a.pool_i = static_cast<int32_t*>(alloc(static_cast<size_t>(chunk) * 2 * kPoolCap * 4));
   a.err = static_cast<int32_t*>(alloc(16));
   unsigned long long* keys = static_cast<unsigned long long*>(alloc(static_cast<size_t>(max_keys) * 8));
   unsigned long long* keys2 = static_cast<unsigned long long*>(alloc(static_cast<size_t>(max_keys) * 8));
   int32_t* heads = static_cast<int32_t*>(alloc(static_cast<size_t>(max_keys) * 4));
+  int32_t* heads2 = static_cast<int32_t*>(alloc(static_cast<size_t>(max_keys) * 4));
   int32_t* nheads = static_cast<int32_t*>(alloc(16));
-  unsigned long long* bump = static_cast<unsigned long long*>(alloc(16));
-  // reverse pools: every overflowing group needs 2 (deg + adds) <= 2 (R + group) entries
-  const int64_t rpool_cap = 2 * (max_keys + static_cast<int64_t>(R) * max_keys);
-  float* rpd = static_cast<float*>(alloc(static_cast<size_t>(rpool_cap) * 4));
-  int32_t* rpi = static_cast<int32_t*>(alloc(static_cast<size_t>(rpool_cap) * 4));
-  size_t sort_bytes = 0;
+  size_t sort_bytes = 0, hsort_bytes = 0;
   cub::DeviceRadixSort::SortKeys(nullptr, sort_bytes, keys, keys2, static_cast<int>(max_keys));
-  void* sort_tmp = alloc(sort_bytes);
+  cub::DeviceRadixSort::SortKeys(nullptr, hsort_bytes, heads, heads2, static_cast<int>(max_keys));
+  void* sort_tmp = alloc(std::max(sort_bytes, hsort_bytes));
+  // reverse-phase pools, grown on demand: (warps) x 2 (R + longest group) entries
+  float* rpd = nullptr;
+  int32_t* rpi = nullptr;
+  uint32_t* rbits = nullptr;
+  int64_t rpool_entries = 0, rbits_words = 0;
   auto cleanup = [&] {
     for (void* p : allocs) cudaFree(p);
+    if (rpd) cudaFree(rpd);
+    if (rpi) cudaFree(rpi);
+    if (rbits) cudaFree(rbits);
   };
   if (!err.empty()) {
     cleanup();
@@ -583,13 +590,12 @@ int run_vamana(const T* h_data, int64_t n, int32_t dim, int32_t R, int32_t L, fl
   ck(cudaMemcpy(d_perm, perm.data(), static_cast<size_t>(n) * 8, cudaMemcpyHostToDevice), "copy order");
   ck(cudaMemset(a.graph, 0xff, static_cast<size_t>(n) * R * 4), "memset");
   ck(cudaMemset(a.degree, 0, static_cast<size_t>(n) * 4), "memset");
-  ck(cudaMemset(a.seen, 0, static_cast<size_t>(kChunk) * kSeenCap * 8), "memset");
+  ck(cudaMemset(a.seen, 0, static_cast<size_t>(chunk) * kSeenCap * 8), "memset");
   ck(cudaMemset(a.err, 0, 16), "memset");
   ck(cudaMemset(a.newdeg, 0, static_cast<size_t>(max_batch) * 4), "memset");
   ck(cudaFuncSetAttribute(search_prune_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                           static_cast<int>(smem)),
      "smem attribute");
-  const size_t rsmem = kWarps * ((kPoolCap + 31) / 32) * 4;
   uint32_t tag = 1;
   for (int32_t pass = 0; pass < passes && err.empty(); ++pass) {
     const float alpha = qv_vamana::pass_alpha(pass, passes, alpha_final);
@@ -598,10 +604,10 @@ int run_vamana(const T* h_data, int64_t n, int32_t dim, int32_t R, int32_t L, fl
     while (start < n && err.empty()) {
       const int64_t end = std::min(n, start + bsize);
       const int64_t cnt = end - start;
-      for (int64_t c0 = 0; c0 < cnt; c0 += kChunk) {
-        const int ch = static_cast<int>(std::min<int64_t>(kChunk, cnt - c0));
+      for (int64_t c0 = 0; c0 < cnt; c0 += chunk) {
+        const int ch = static_cast<int>(std::min<int64_t>(chunk, cnt - c0));
         if (tag + static_cast<uint32_t>(ch) < tag) {  // tags wrapped: clear the sets
-          ck(cudaMemset(a.seen, 0, static_cast<size_t>(kChunk) * kSeenCap * 8), "memset");
+          ck(cudaMemset(a.seen, 0, static_cast<size_t>(chunk) * kSeenCap * 8), "memset");
           tag = 1;
         }
         search_prune_kernel<T><<<(ch + kWarps - 1) / kWarps, kWarps * 32, smem>>>(a, start + c0, ch, c0, tag,
@@ -611,19 +617,43 @@ int run_vamana(const T* h_data, int64_t n, int32_t dim, int32_t R, int32_t L, fl
       const int64_t total = cnt * R;
       install_kernel<<<static_cast<unsigned>((total + 255) / 256), 256>>>(a, start, cnt, keys);
       cub::DeviceRadixSort::SortKeys(sort_tmp, sort_bytes, keys, keys2, static_cast<int>(total));
-      RevArgs r{keys2, total, heads, nheads, bump, rpd, rpi, rpool_cap};
       ck(cudaMemsetAsync(nheads, 0, 16), "memset");
-      ck(cudaMemsetAsync(bump, 0, 16), "memset");
-      heads_kernel<<<static_cast<unsigned>((total + 255) / 256), 256>>>(r);
-      reverse_kernel<T><<<std::max<int64_t>(1, std::min<int64_t>((total + kWarps - 1) / kWarps, 65535)),
-                          kWarps * 32, rsmem>>>(a, r, alpha);
+      heads_kernel<<<static_cast<unsigned>((total + 255) / 256), 256>>>(keys2, total, heads, nheads);
+      int32_t nh[3] = {0, 0, 0};
+      ck(cudaMemcpy(nh, nheads, 12, cudaMemcpyDeviceToHost), "group count");
+      if (nh[0] > 0) {
+        cub::DeviceRadixSort::SortKeys(sort_tmp, hsort_bytes, heads, heads2, nh[0]);
+        longest_kernel<<<static_cast<unsigned>((nh[0] + 255) / 256), 256>>>(heads2, nheads);
+        ck(cudaMemcpy(nh, nheads, 12, cudaMemcpyDeviceToHost), "longest group");
+        const int64_t per_warp = 2 * (static_cast<int64_t>(R) + nh[2]);
+        // as many warps as groups, at most 16 per SM, within ~4 GB of pools
+        int64_t warps = std::min<int64_t>(nh[0], static_cast<int64_t>(num_sms) * 16);
+        warps = std::max<int64_t>(kWarps, std::min<int64_t>(warps, (int64_t(4) << 30) / (8 * per_warp)));
+        warps = (warps + kWarps - 1) / kWarps * kWarps;
+        const int64_t bits_per_warp = (R + static_cast<int64_t>(nh[2]) + 31) / 32;
+        if (warps * per_warp > rpool_entries || warps * bits_per_warp > rbits_words) {
+          if (rpd) cudaFree(rpd);
+          if (rpi) cudaFree(rpi);
+          if (rbits) cudaFree(rbits);
+          rpd = nullptr;
+          rpi = nullptr;
+          rbits = nullptr;
+          rpool_entries = warps * per_warp;
+          rbits_words = warps * bits_per_warp;
+          if (!ck(cudaMalloc(&rpd, static_cast<size_t>(rpool_entries) * 4), "cudaMalloc") ||
+              !ck(cudaMalloc(&rpi, static_cast<size_t>(rpool_entries) * 4), "cudaMalloc") ||
+              !ck(cudaMalloc(&rbits, static_cast<size_t>(rbits_words) * 4), "cudaMalloc"))
+            break;
+        }
+        RevArgs r{keys2, total, heads2, nheads, rpd, rpi, rbits, per_warp, bits_per_warp};
+        reverse_kernel<T><<<static_cast<unsigned>(warps / kWarps), kWarps * 32>>>(a, r, alpha);
+      }
       int32_t e[2] = {0, 0};
       ck(cudaMemcpy(e, a.err, 8, cudaMemcpyDeviceToHost), "build kernels");
       if (e[0] != kBuildOk && err.empty())
         err = e[0] == kErrExpansions ? "a greedy search expanded more than " + std::to_string(kExpCap) +
                                            " nodes (point " + std::to_string(e[1]) + ")"
-              : e[0] == kErrSeen    ? "a greedy search saw more than " + std::to_string(kSeenCap) + " nodes"
-                                    : "reverse-edge pool space exhausted";
+                                     : "a greedy search saw more than " + std::to_string(kSeenCap) + " nodes";
       start = end;
       bsize = std::min(max_batch, bsize * 2);
     }

@@ -66,7 +66,7 @@ def _headers() -> list[Path]:
 
 def build_engine(force: bool = False, verbose: bool = False) -> Path:
     """Compile libquiver_b200.so (sm_100a)."""
-    units = ["engine.cu", "search_u8.cu", "search_i8.cu", "search_f32.cu", "adc_batch.cu", "vamana_gpu.cu", "index_io.cpp"]
+    units = ["engine.cu", "search_u8.cu", "search_i8.cu", "search_f32.cu", "adc_batch.cu", "vamana_gpu.cu", "build_gpu.cu", "index_io.cpp"]
     headers = _headers()
     if not force and ENGINE_LIB.exists() and not _newer(ENGINE_LIB, [CSRC / u for u in units] + headers):
         return ENGINE_LIB

@@ -113,6 +113,10 @@ ENGINE_SYMBOLS = {
     "qv_adc_device": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_void_p, C.c_void_p]),
     "qv_exact_l2_device": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_void_p,
                                      C.c_void_p]),
+    "qv_synth_mixture_gpu": (C.c_int, [C.c_uint64, C.c_int32, C.c_int64, C.c_int64, C.c_int64, C.c_int64,
+                                       C.c_double, C.c_int32, C.c_void_p, C.c_int32]),
+    "qv_pq_encode_gpu": (C.c_int, [C.c_void_p, C.c_int64, C.c_int64, C.c_int32, C.c_int32, C.c_void_p, C.c_void_p,
+                                   C.c_void_p, C.c_int32, C.c_void_p]),
     "qv_vamana_gpu": (C.c_int, [C.c_void_p, C.c_int64, C.c_int64, C.c_int32, C.c_int32, C.c_int32, C.c_float,
                                 C.c_int32, C.c_uint64, C.c_int32, C.c_void_p, C.c_void_p, C.POINTER(C.c_int64)]),
     "qv_adc_batch": (C.c_int, [C.c_void_p, C.c_int64, C.c_int32, C.c_void_p, C.c_int64, C.c_void_p, C.c_void_p,

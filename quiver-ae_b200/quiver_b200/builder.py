@@ -26,10 +26,16 @@ def _ptr(a: np.ndarray) -> C.c_void_p:
 
 
 def synth_mixture(seed: int, n: int, dim: int, n_centers: int, sigma: float, data_type: str = "uint8",
-                  stream: int = 0, row0: int = 0, nthreads: int = 0) -> np.ndarray:
-    """Rows [row0, row0+n) of the seeded mixture (stream 0 = base, 1 = queries)."""
+                  stream: int = 0, row0: int = 0, nthreads: int = 0, device: int | None = None) -> np.ndarray:
+    """Rows [row0, row0+n) of the seeded mixture (stream 0 = base, 1 = queries); on GPU `device`
+    when given (the same bits)."""
     dt = formats.NUMPY_DTYPES[data_type]
     out = np.empty((n, dim), dtype=dt)
+    if device is not None:
+        from . import engine
+        engine._check(_lib.engine_lib().qv_synth_mixture_gpu(seed, stream, row0, n, dim, n_centers, sigma,
+                                                             _lib.DTYPE_CODES[data_type], _ptr(out), device))
+        return out
     _check(_lib.index_lib().qvb_synth_mixture(seed, stream, row0, n, dim, n_centers, sigma,
                                                _lib.DTYPE_CODES[data_type], _ptr(out), nthreads))
     return out
@@ -85,13 +91,20 @@ def pq_train(base: np.ndarray, M: int, sample: int = 100_000, iters: int = 12, s
 
 
 def pq_encode(base: np.ndarray, pivots: np.ndarray, centroid: np.ndarray, chunk_offsets: np.ndarray,
-              nthreads: int = 0) -> np.ndarray:
+              nthreads: int = 0, device: int | None = None) -> np.ndarray:
     base = np.ascontiguousarray(base)
     n, dim = base.shape
     M = len(chunk_offsets) - 1
     dtype = {np.dtype(np.uint8): _lib.QV_UINT8, np.dtype(np.int8): _lib.QV_INT8,
              np.dtype(np.float32): _lib.QV_FLOAT}[base.dtype]
     codes = np.empty((n, M), dtype=np.uint8)
+    if device is not None:
+        from . import engine
+        engine._check(_lib.engine_lib().qv_pq_encode_gpu(
+            _ptr(base), n, dim, dtype, M, _ptr(np.ascontiguousarray(pivots, dtype=np.float32)),
+            _ptr(np.ascontiguousarray(centroid, dtype=np.float32)),
+            _ptr(np.ascontiguousarray(chunk_offsets, dtype=np.int32)), device, _ptr(codes)))
+        return codes
     _check(_lib.index_lib().qvb_pq_encode(_ptr(base), n, dim, dtype, M,
                                            _ptr(np.ascontiguousarray(pivots, dtype=np.float32)),
                                            _ptr(np.ascontiguousarray(centroid, dtype=np.float32)),
@@ -118,20 +131,20 @@ def vamana_gpu(base: np.ndarray, R: int, L: int, alpha: float, passes: int = 2, 
 
 def build_index(index_dir: str | Path, base: np.ndarray, *, R: int = 64, L: int = 100, alpha: float = 1.2,
                 M: int = 32, passes: int = 2, pq_sample: int = 100_000, pq_iters: int = 12, seed: int = 0,
-                prefix: str = "ann", nthreads: int = 0, graph_device: int | None = None) -> BuiltIndex:
+                prefix: str = "ann", nthreads: int = 0, device: int | None = None) -> BuiltIndex:
     """Write ``<prefix>_disk.index``, ``<prefix>_pq_pivots.bin`` and ``<prefix>_pq_compressed.bin``.
-    graph_device: build the graph on that GPU (the same graph as the host builder's)."""
+    device: build the graph and encode the codes on that GPU (the same files as the host build)."""
     index_dir = Path(index_dir)
     index_dir.mkdir(parents=True, exist_ok=True)
     base = np.ascontiguousarray(base)
     data_type = {np.dtype(np.uint8): "uint8", np.dtype(np.int8): "int8", np.dtype(np.float32): "float"}[base.dtype]
-    if graph_device is None:
+    if device is None:
         graph, degree, medoid = vamana(base, R, L, alpha, passes, seed, nthreads)
     else:
-        graph, degree, medoid = vamana_gpu(base, R, L, alpha, passes, seed, graph_device)
+        graph, degree, medoid = vamana_gpu(base, R, L, alpha, passes, seed, device)
     layout = formats.write_disk_index(index_dir / f"{prefix}_disk.index", base, graph, degree, medoid, R)
     pivots, centroid, offs = pq_train(base, M, pq_sample, pq_iters, seed, nthreads)
-    codes = pq_encode(base, pivots, centroid, offs, nthreads)
+    codes = pq_encode(base, pivots, centroid, offs, nthreads, device=device)
     formats.write_pq(index_dir / prefix, pivots, centroid, offs, codes)
     return BuiltIndex(index_dir, index_dir / prefix, data_type, layout)
 

@@ -45,6 +45,9 @@ CONFIGS = {
     "config0": Workload("config0", 1_000_000, 128, "uint8", 1000, 20.0, 64, 100, 1.2, 32, 10_000, 10, 45),
     # 10M x 96-d float32 unit-normalised, 5000 clusters (sigma 0.1), R=64, PQ 32 x 256.
     "config1": Workload("config1", 10_000_000, 96, "float", 5000, 0.1, 64, 100, 1.2, 32, 10_000, 10, 45),
+    # 100M x 128-d uint8 mixture as config 0 with 10K clusters, R=64, PQ 32 x 256 (3.2 GB of
+    # codes, 41 GB of graph pages -- both fit one B200's HBM), 100K queries per step, top-10.
+    "config2": Workload("config2", 100_000_000, 128, "uint8", 10_000, 20.0, 64, 100, 1.2, 32, 100_000, 10, 45),
     # small shapes of config0 for tests and smoke runs
     "config0-100k": Workload("config0-100k", 100_000, 128, "uint8", 100, 20.0, 64, 100, 1.2, 32, 10_000, 10, 45),
     "config0-20k": Workload("config0-20k", 20_000, 128, "uint8", 20, 20.0, 64, 100, 1.2, 32, 2_000, 10, 45),
@@ -59,31 +62,44 @@ def index_dir(w: Workload) -> Path:
     return cache_root() / f"{w.name}-s{w.seed}"
 
 
-def queries(w: Workload, rows: int | None = None, row0: int = 0) -> np.ndarray:
+def queries(w: Workload, rows: int | None = None, row0: int = 0, device: int | None = None) -> np.ndarray:
     n = w.nq if rows is None else rows
-    return builder.synth_mixture(w.seed, n, w.dim, w.centers, w.sigma, w.data_type, stream=1, row0=row0)
+    return builder.synth_mixture(w.seed, n, w.dim, w.centers, w.sigma, w.data_type, stream=1, row0=row0,
+                                 device=device)
 
 
-def base(w: Workload) -> np.ndarray:
-    return builder.synth_mixture(w.seed, w.n, w.dim, w.centers, w.sigma, w.data_type, stream=0)
+def base(w: Workload, device: int | None = None) -> np.ndarray:
+    """The base set; generated on GPU `device` when given (the same bits as on the host)."""
+    return builder.synth_mixture(w.seed, w.n, w.dim, w.centers, w.sigma, w.data_type, stream=0, device=device)
 
 
-def prepare(w: Workload, log=print) -> Path:
-    """Build (or reuse) the index of `w`; returns its directory."""
+def prepare(w: Workload, log=print, device: int | None = None) -> Path:
+    """Build (or reuse) the index of `w`; returns its directory.  With a GPU `device` the data, the graph and
+    the PQ codes are produced there (the same files as the host build)."""
     d = index_dir(w)
     stamp = d / "workload.json"
     if stamp.exists() and json.loads(stamp.read_text()) == asdict(w):
         return d
     d.mkdir(parents=True, exist_ok=True)
     t0 = time.time()
-    b = base(w)
-    log(f"[workload] {w.name}: synthesised {w.n} x {w.dim} {w.data_type} in {time.time() - t0:.1f}s")
+    b = base(w, device)
+    where = "host" if device is None else f"GPU {device}"
+    log(f"[workload] {w.name}: synthesised {w.n} x {w.dim} {w.data_type} on {where} in {time.time() - t0:.1f}s")
     t0 = time.time()
     builder.build_index(d, b, R=w.R, L=w.L, alpha=w.alpha, M=w.M, passes=w.passes, pq_sample=w.pq_sample,
-                        seed=w.seed)
-    log(f"[workload] {w.name}: Vamana R={w.R} L={w.L} alpha={w.alpha} + PQ M={w.M} built in {time.time() - t0:.1f}s")
+                        seed=w.seed, device=device)
+    build_s = time.time() - t0
+    log(f"[workload] {w.name}: Vamana R={w.R} L={w.L} alpha={w.alpha} + PQ M={w.M} built on {where} in "
+        f"{build_s:.1f}s")
+    (d / "build.json").write_text(json.dumps({"where": where, "seconds": build_s}))
     stamp.write_text(json.dumps(asdict(w)))
     return d
+
+
+def build_info(w: Workload) -> dict | None:
+    """Where and how fast the cached index of `w` was built (None if unknown)."""
+    p = index_dir(w) / "build.json"
+    return json.loads(p.read_text()) if p.exists() else None
 
 
 def prepare_nav(w: Workload, log=print) -> Path:
@@ -108,10 +124,11 @@ def ground_truth(w: Workload, q: np.ndarray, k: int = 10, device: str | None = N
     key = d / f"gt_{q.shape[0]}_{k}_{hashlib.sha1(q.tobytes()).hexdigest()[:12]}.ibin"
     if key.exists():
         return formats.read_bin(key, np.int32)
-    b = base(w)
     if device is None:
+        b = base(w)
         ids, _ = builder.ground_truth(b, q, k)
     else:
+        b = base(w, int(str(device).split(":")[-1]))
         ids = _gt_torch(b, q, k, device)
     formats.write_bin(key, ids)
     return ids

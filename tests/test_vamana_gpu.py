@@ -68,7 +68,7 @@ def test_gpu_built_index_searches_like_host_built(tmp_path):
     base = builder.synth_mixture(21, 20000, 128, 20, 20.0, "uint8")
     q = builder.synth_mixture(21, 200, 128, 20, 20.0, "uint8", stream=1).astype(np.float32)
     gt, _ = builder.ground_truth(base, q.astype(np.uint8), 10)
-    builder.build_index(tmp_path / "g", base, R=64, L=100, M=32, pq_sample=20000, seed=1, graph_device=0)
+    builder.build_index(tmp_path / "g", base, R=64, L=100, M=32, pq_sample=20000, seed=1, device=0)
     builder.build_index(tmp_path / "h", base, R=64, L=100, M=32, pq_sample=20000, seed=1)
     p = SearchParams(topk=10, ef_search=200, early_exit_policy="none")
     with Engine.open(tmp_path / "g", "uint8") as eng:
@@ -79,3 +79,23 @@ def test_gpu_built_index_searches_like_host_built(tmp_path):
     np.testing.assert_array_equal(d_g.view(np.uint32), d_h.view(np.uint32))
     recall = np.mean([len(set(a) & set(b)) / 10 for a, b in zip(ids_g, gt)])
     assert recall >= 0.85
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype,dim,sigma", [("uint8", 128, 20.0), ("float", 96, 0.1), ("uint8", 37, 30.0)])
+def test_gpu_synth_equals_host(dtype, dim, sigma):
+    from quiver_b200 import builder
+    for stream, row0 in ((0, 0), (1, 12345)):
+        h = builder.synth_mixture(7, 3000, dim, 50, sigma, dtype, stream=stream, row0=row0)
+        g = builder.synth_mixture(7, 3000, dim, 50, sigma, dtype, stream=stream, row0=row0, device=0)
+        np.testing.assert_array_equal(g.view(np.uint8), h.view(np.uint8))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype,dim,M", [("uint8", 128, 32), ("float", 96, 32), ("uint8", 50, 12)])
+def test_gpu_pq_encode_equals_host(dtype, dim, M):
+    from quiver_b200 import builder
+    base = builder.synth_mixture(8, 20000, dim, 40, 20.0 if dtype == "uint8" else 0.1, dtype)
+    piv, cen, offs = builder.pq_train(base, M, sample=5000, iters=4, seed=1)
+    np.testing.assert_array_equal(builder.pq_encode(base, piv, cen, offs, device=0),
+                                  builder.pq_encode(base, piv, cen, offs))
