@@ -70,40 +70,54 @@ def node_size_for(dim: int, dtype, R: int) -> int:
     return dim * np.dtype(dtype).itemsize + 4 * (R + 1)
 
 
-def build_pages(data: np.ndarray, graph: np.ndarray, degree: np.ndarray, R: int) -> tuple[np.ndarray, int, int]:
-    """Node records packed into 4 KB pages -> (pages [P x 4096] u8, node_size, npp)."""
-    n, dim = data.shape
-    data_size = dim * data.dtype.itemsize
+def _page_geometry(data: np.ndarray, R: int) -> tuple[int, int, int]:
+    data_size = data.shape[1] * data.dtype.itemsize
     node_size = data_size + 4 * (R + 1)
     npp = PAGE // node_size
     if npp < 1:
         raise ValueError("a node record does not fit in a 4 KB page")
-    rec = np.zeros((n, node_size), dtype=np.uint8)
-    rec[:, :data_size] = np.ascontiguousarray(data).view(np.uint8).reshape(n, data_size)
-    rec[:, data_size:data_size + 4] = degree.astype("<u4").view(np.uint8).reshape(n, 4)
-    nb = np.where(np.arange(R)[None, :] < degree[:, None], graph[:, :R], 0).astype("<u4")
-    rec[:, data_size + 4:] = nb.view(np.uint8).reshape(n, 4 * R)
-    num_pages = (n + npp - 1) // npp
-    pages = np.zeros((num_pages, PAGE), dtype=np.uint8)
+    return data_size, node_size, npp
+
+
+def _pages_of(data: np.ndarray, graph: np.ndarray, degree: np.ndarray, R: int, n0: int, n1: int) -> np.ndarray:
+    """Pages holding nodes [n0, n1) (n0 a multiple of nodes-per-page)."""
+    data_size, node_size, npp = _page_geometry(data, R)
+    m = n1 - n0
+    num_pages = (m + npp - 1) // npp
     full = np.zeros((num_pages * npp, node_size), dtype=np.uint8)
-    full[:n] = rec
+    full[:m, :data_size] = np.ascontiguousarray(data[n0:n1]).view(np.uint8).reshape(m, data_size)
+    deg = np.asarray(degree[n0:n1])
+    full[:m, data_size:data_size + 4] = deg.astype("<u4").view(np.uint8).reshape(m, 4)
+    nb = np.where(np.arange(R)[None, :] < deg[:, None], graph[n0:n1, :R], 0).astype("<u4")
+    full[:m, data_size + 4:] = nb.view(np.uint8).reshape(m, 4 * R)
+    pages = np.zeros((num_pages, PAGE), dtype=np.uint8)
     pages[:, :npp * node_size] = full.reshape(num_pages, npp * node_size)
-    return pages, node_size, npp
+    return pages
+
+
+def build_pages(data: np.ndarray, graph: np.ndarray, degree: np.ndarray, R: int) -> tuple[np.ndarray, int, int]:
+    """Node records packed into 4 KB pages -> (pages [P x 4096] u8, node_size, npp)."""
+    _, node_size, npp = _page_geometry(data, R)
+    return _pages_of(data, graph, degree, R, 0, data.shape[0]), node_size, npp
 
 
 def write_disk_index(path: str | Path, data: np.ndarray, graph: np.ndarray, degree: np.ndarray,
-                     medoid: int, R: int) -> DiskLayout:
+                     medoid: int, R: int, nodes_per_slice: int = 1 << 20) -> DiskLayout:
+    """Header page, then the node pages, written a slice of nodes at a time (bounded memory at any n)."""
     n, dim = data.shape
-    pages, node_size, npp = build_pages(data, graph, degree, R)
-    file_size = PAGE * (pages.shape[0] + 1)
+    _, node_size, npp = _page_geometry(data, R)
+    num_pages = (n + npp - 1) // npp
+    file_size = PAGE * (num_pages + 1)
     meta = [n, dim, medoid, node_size, npp, 0, 0, 0, file_size]
     header = np.zeros(PAGE, dtype=np.uint8)
     hb = struct.pack("<II", len(meta), 1) + struct.pack(f"<{len(meta)}Q", *meta)
     header[:len(hb)] = np.frombuffer(hb, dtype=np.uint8)
+    step = max(npp, nodes_per_slice // npp * npp)
     with open(path, "wb") as f:
-        f.write(header.tobytes())
-        f.write(pages.tobytes())
-    return DiskLayout(n, dim, medoid, node_size, npp, dim * data.dtype.itemsize, R, pages.shape[0])
+        header.tofile(f)
+        for n0 in range(0, n, step):
+            _pages_of(data, graph, degree, R, n0, min(n, n0 + step)).tofile(f)
+    return DiskLayout(n, dim, medoid, node_size, npp, dim * data.dtype.itemsize, R, num_pages)
 
 
 def read_disk_index_header(path: str | Path, data_type: str) -> DiskLayout:
