@@ -287,6 +287,9 @@ def main() -> int:
                     help="also time small batches end to end, e.g. 1,4,16 (latency mode; rank 0 only)")
     ap.add_argument("--stripe-devices", default="",
                     help="stripe the page store over these GPUs, e.g. 0,1 (pages p mod S; peer loads)")
+    ap.add_argument("--stripe-shared", action="store_true",
+                    help="under torchrun: rank r holds pages p = r (mod N) and reads the rest from the other "
+                         "ranks' GPUs (CUDA IPC, peer loads)")
     ap.add_argument("--visited-filter", action="store_true",
                     help="the engine's visited-filter mode (not reference behaviour; reports its recall)")
     ap.add_argument("--nav", action="store_true",
@@ -345,7 +348,9 @@ def main() -> int:
     barrier()
     d = workloads.index_dir(w)
     stripes = [int(x) for x in args.stripe_devices.split(",") if x]
-    if stripes:
+    if args.stripe_shared:
+        eng = shard.open_shared(d, w.data_type, device=local)
+    elif stripes:
         eng = Engine.open(d, w.data_type, device=local, page_store="striped", stripe_devices=stripes)
     else:
         eng = Engine.open(d, w.data_type, device=local)
@@ -478,7 +483,10 @@ def main() -> int:
                              f"{info.num_points * info.num_chunks / 1e6:.0f} MB vs 126 MB L2, no flush",
                        "parallelism": f"query shards x{world}, index replicated",
                        "index_build": workloads.build_info(w),
-                       "page_store": f"striped over GPUs {stripes} (peer loads)" if stripes else "HBM of the search GPU"},
+                       "page_store": (f"shared: rank r holds pages p = r mod {world}, the rest read from the other "
+                                      f"ranks' GPUs (CUDA IPC peer loads)" if args.stripe_shared
+                                      else f"striped over GPUs {stripes} (peer loads)" if stripes
+                                      else "HBM of the search GPU")},
             "recall_at_10": recall,
             "p50_ms": streaming["p50_ms"] if streaming else p50,
             "p99_ms": streaming["p99_ms"] if streaming else p99,
@@ -506,6 +514,8 @@ def main() -> int:
         if not args.no_adc:
             line["adc_batch"] = adc_microbench(dev, stream, peaks["hbm_gbs"])
         print(json.dumps(line), flush=True)
+    if args.stripe_shared:
+        barrier()  # every rank reads every other rank's stripe: close only when all are done
     eng.close()
     if world > 1:
         dist.destroy_process_group()

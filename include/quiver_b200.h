@@ -46,6 +46,10 @@ extern "C" {
 #define QV_PAGES_STRIPED 2  /* page p on stripe p mod S of S devices' HBM (S = 1, 2, 4 or 8, see
                                qv_engine_opts.stripe_devices); the search GPU reads the other
                                stripes with peer loads over NVLink / NVSwitch */
+#define QV_PAGES_SHARED 3   /* the same striping across S processes, one per GPU: this engine
+                               holds stripe stripe_rank in its own GPU's HBM and reads the
+                               others from the processes that hold them (CUDA IPC); see
+                               qv_engine_stripe_handle / qv_engine_attach_stripes */
 
 /* Early-exit policy (src/quiver/io_control.cuh:41-46; the CLI accepts only
  * "none" and "gpruning", bin/quiver_search.cu:48-54). */
@@ -87,6 +91,7 @@ typedef struct {
   int32_t num_stripes;            /* QV_PAGES_STRIPED: S, a power of two <= 8 */
   const int32_t* stripe_devices;  /* QV_PAGES_STRIPED: [S] CUDA ordinals (repeats allowed); every one
                                      must be `device` or peer-accessible from it */
+  int32_t stripe_rank;            /* QV_PAGES_SHARED: the stripe this engine holds, in [0, S) */
 } qv_engine_opts;
 
 /* Index arrays already in host memory, in the on-disk layouts:
@@ -260,6 +265,18 @@ int qv_check_device_status(qv_engine* engine);
 int qv_search_noalloc(qv_engine* engine, const float* queries, int64_t nq, int64_t dim,
                       const qv_search_opts* opts, int32_t* ids, float* dists,
                       int32_t* found);
+
+/* Page store shared by S processes (QV_PAGES_SHARED).  After
+ * qv_engine_create, every process exports its stripe with
+ * qv_engine_stripe_handle (QV_STRIPE_HANDLE_BYTES of CUDA IPC handle), the
+ * processes exchange the handles (any host channel: the caller's process
+ * group), and each passes all S handles, in stripe order, to
+ * qv_engine_attach_stripes; searches are refused until then.  A process must
+ * keep its engine alive while others may still search (destroy the engines
+ * after a barrier). */
+#define QV_STRIPE_HANDLE_BYTES 64
+int qv_engine_stripe_handle(qv_engine* engine, void* handle);
+int qv_engine_attach_stripes(qv_engine* engine, const void* handles);
 
 /* Launch geometry qv_search_device would use (grid, slots, smem). */
 int qv_plan(qv_engine* engine, const qv_search_opts* opts, int64_t nq,

@@ -73,6 +73,11 @@ struct qv_engine {
   std::vector<uint8_t*> stripe_ptr;
   uint8_t** d_stripe_table = nullptr;
   int stripe_shift = 0;
+  // QV_PAGES_SHARED: this process holds stripe stripe_rank; the others are
+  // other processes' allocations opened by IPC (closed, not freed, here)
+  bool shared = false, attached = false;
+  int stripe_rank = -1;
+  std::vector<void*> imported;
   uint8_t* h_pages = nullptr;   // pinned mapped host allocation (host store)
   uint8_t* d_codes = nullptr;
   float* d_pivots_t = nullptr;
@@ -122,8 +127,9 @@ struct qv_engine {
     } else if (d_pages && stripe_ptr.empty()) {  // with stripes, d_pages is stripe 0
       cudaFree(d_pages);
     }
+    for (void* p : imported) cudaIpcCloseMemHandle(p);
     for (size_t s = 0; s < stripe_ptr.size(); ++s) {
-      if (!stripe_ptr[s]) continue;
+      if (!stripe_ptr[s] || (shared && static_cast<int>(s) != stripe_rank)) continue;
       cudaSetDevice(stripe_dev[s]);
       cudaFree(stripe_ptr[s]);
     }
@@ -147,6 +153,8 @@ namespace {
 using qv::Plan;
 
 void validate_opts(const qv_engine* e, const qv_search_opts& o) {
+  if (e->shared && !e->attached)
+    fail(QV_ERR_INVALID_ARG, "a shared page store needs every process's stripe (qv_engine_attach_stripes) first");
   if (o.topk < 1 || o.topk > 1024) fail(QV_ERR_INVALID_ARG, "topk must be in [1, 1024]");
   if (o.ef_search < 1 || o.ef_search > 4096) fail(QV_ERR_INVALID_ARG, "ef_search must be in [1, 4096]");
   if (o.pipe_width < 1 || o.pipe_width > qvk::kMaxPipeWidth)
@@ -410,8 +418,8 @@ void alloc_pages(qv_engine* e, int32_t page_store) {
     CK(cudaHostGetDevicePointer(reinterpret_cast<void**>(&e->d_pages), e->h_pages, 0));
   } else if (page_store == QV_PAGES_HBM) {
     CK(cudaMalloc(&e->d_pages, bytes));
-  } else if (page_store != QV_PAGES_STRIPED) {
-    fail(QV_ERR_INVALID_ARG, "page_store must be QV_PAGES_HBM, QV_PAGES_HOST or QV_PAGES_STRIPED");
+  } else if (page_store != QV_PAGES_STRIPED && page_store != QV_PAGES_SHARED) {
+    fail(QV_ERR_INVALID_ARG, "page_store must be QV_PAGES_HBM, QV_PAGES_HOST, QV_PAGES_STRIPED or QV_PAGES_SHARED");
   }
 }
 
@@ -458,6 +466,27 @@ void stripe_pages(qv_engine* e, const uint8_t* host_pages, int32_t num_stripes, 
   CK(cudaMemcpy(e->d_stripe_table, e->stripe_ptr.data(), sizeof(uint8_t*) * num_stripes, cudaMemcpyHostToDevice));
   e->stripe_shift = shift;
   e->d_pages = e->stripe_ptr[0];  // stripe 0 (the whole store when S == 1)
+}
+
+// QV_PAGES_SHARED: this process's stripe only (pages p = rank, rank + S, ...),
+// read straight from the page file; the table is built at attach time.
+void load_own_stripe(qv_engine* e, const std::string& page_file, int32_t num_stripes, int32_t rank) {
+  if (num_stripes < 1 || num_stripes > 8 || (num_stripes & (num_stripes - 1)) != 0)
+    fail(QV_ERR_INVALID_ARG, "num_stripes must be 1, 2, 4 or 8");
+  if (rank < 0 || rank >= num_stripes) fail(QV_ERR_INVALID_ARG, "stripe_rank must be in [0, num_stripes)");
+  const int64_t P = e->L.num_pages;
+  const int64_t n = P > rank ? (P - rank + num_stripes - 1) / num_stripes : 0;
+  std::vector<uint8_t> host(static_cast<size_t>(std::max<int64_t>(n, 1)) * qv::kPage);
+  qv::read_stripe_pages(page_file, P, num_stripes, rank, host.data());
+  int shift = 0;
+  while ((1 << shift) < num_stripes) ++shift;
+  e->shared = true;
+  e->stripe_rank = rank;
+  e->stripe_shift = shift;
+  e->stripe_dev.assign(num_stripes, e->device);
+  e->stripe_ptr.assign(num_stripes, nullptr);
+  CK(cudaMalloc(&e->stripe_ptr[rank], host.size()));
+  CK(cudaMemcpy(e->stripe_ptr[rank], host.data(), static_cast<size_t>(n) * qv::kPage, cudaMemcpyHostToDevice));
 }
 
 void ensure_staging(qv_engine* e, int64_t nq, int64_t k) {
@@ -609,6 +638,9 @@ int qv_engine_create(const qv_engine_opts* opts, qv_engine** out) {
         const int64_t b = qv::validate_adjacency(e->L, e->h_pages);
         if (b >= 0) fail(QV_ERR_BAD_INDEX, "adjacency list of node " + std::to_string(b) + " is malformed");
       }
+    } else if (opts->page_store == QV_PAGES_SHARED) {
+      if (opts->validate) fail(QV_ERR_INVALID_ARG, "validate needs the whole page store, not one stripe");
+      load_own_stripe(e.get(), page_file, opts->num_stripes, opts->stripe_rank);
     } else {
       std::vector<uint8_t> host(bytes);
       qv::read_pages(page_file, e->L.num_pages, backend, host.data());
@@ -725,6 +757,44 @@ int qv_engine_info(const qv_engine* e, qv_index_info* info) {
 }
 
 void qv_engine_destroy(qv_engine* e) { delete e; }
+
+int qv_engine_stripe_handle(qv_engine* e, void* handle) {
+  return guarded([&] {
+    if (!e || !handle) fail(QV_ERR_INVALID_ARG, "null argument");
+    if (!e->shared) fail(QV_ERR_INVALID_ARG, "the engine's page store is not QV_PAGES_SHARED");
+    static_assert(sizeof(cudaIpcMemHandle_t) == QV_STRIPE_HANDLE_BYTES, "IPC handle size");
+    CK(cudaSetDevice(e->device));
+    cudaIpcMemHandle_t h;
+    CK(cudaIpcGetMemHandle(&h, e->stripe_ptr[e->stripe_rank]));
+    std::memcpy(handle, &h, sizeof(h));
+  });
+}
+
+int qv_engine_attach_stripes(qv_engine* e, const void* handles) {
+  return guarded([&] {
+    if (!e || !handles) fail(QV_ERR_INVALID_ARG, "null argument");
+    if (!e->shared) fail(QV_ERR_INVALID_ARG, "the engine's page store is not QV_PAGES_SHARED");
+    if (e->attached) fail(QV_ERR_INVALID_ARG, "stripes are already attached");
+    CK(cudaSetDevice(e->device));
+    const int S = static_cast<int>(e->stripe_ptr.size());
+    for (int s = 0; s < S; ++s) {
+      if (s == e->stripe_rank) continue;
+      cudaIpcMemHandle_t h;
+      std::memcpy(&h, static_cast<const uint8_t*>(handles) + static_cast<size_t>(s) * QV_STRIPE_HANDLE_BYTES,
+                  sizeof(h));
+      void* p = nullptr;
+      const cudaError_t r = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+      if (r != cudaSuccess)
+        fail(QV_ERR_CUDA, "opening stripe " + std::to_string(s) + ": " + cudaGetErrorString(r));
+      e->imported.push_back(p);
+      e->stripe_ptr[s] = static_cast<uint8_t*>(p);
+    }
+    CK(cudaMalloc(&e->d_stripe_table, sizeof(uint8_t*) * S));
+    CK(cudaMemcpy(e->d_stripe_table, e->stripe_ptr.data(), sizeof(uint8_t*) * S, cudaMemcpyHostToDevice));
+    e->d_pages = e->stripe_ptr[0];
+    e->attached = true;
+  });
+}
 
 int qv_plan(qv_engine* e, const qv_search_opts* opts, int64_t nq, qv_search_stats* plan) {
   return guarded([&] {
@@ -1161,6 +1231,8 @@ int qv_exact_l2_device(qv_engine* e, const float* d_q2, const int32_t* d_qof, co
                        float* d_out, void* stream) {
   return guarded([&] {
     if (!e || (n > 0 && (!d_q2 || !d_qof || !d_ids || !d_out))) fail(QV_ERR_INVALID_ARG, "null argument");
+    if (e->shared && !e->attached)
+      fail(QV_ERR_INVALID_ARG, "a shared page store needs every process's stripe (qv_engine_attach_stripes) first");
     CK(cudaSetDevice(e->device));
     if (n <= 0) return;
     qvk::SearchParams p{};

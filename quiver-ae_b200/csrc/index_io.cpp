@@ -209,6 +209,28 @@ void read_pages(const std::string& path, int64_t num_pages, const std::string& b
   ::close(fd);
 }
 
+void read_stripe_pages(const std::string& path, int64_t num_pages, int32_t num_stripes, int32_t rank,
+                       uint8_t* dst) {
+  const int fd = ::open(path.c_str(), O_RDONLY);
+  if (fd < 0) throw IoError(QV_ERR_IO, "Failed to open page file " + path);
+  struct stat st {};
+  if (fstat(fd, &st) != 0 || st.st_size < (num_pages + 1) * kPage) {
+    ::close(fd);
+    throw IoError(QV_ERR_BAD_INDEX, "page file " + path + " is too small");
+  }
+  void* m = mmap(nullptr, static_cast<size_t>(st.st_size), PROT_READ, MAP_PRIVATE, fd, 0);
+  if (m == MAP_FAILED) {
+    ::close(fd);
+    throw IoError(QV_ERR_IO, "Failed to map page file " + path);
+  }
+  const uint8_t* src = static_cast<const uint8_t*>(m) + kPage;
+  int64_t j = 0;
+  for (int64_t p = rank; p < num_pages; p += num_stripes, ++j)
+    std::memcpy(dst + static_cast<size_t>(j) * kPage, src + static_cast<size_t>(p) * kPage, kPage);
+  munmap(m, static_cast<size_t>(st.st_size));
+  ::close(fd);
+}
+
 int64_t validate_adjacency(const Layout& L, const uint8_t* pages) {
   for (int64_t v = 0; v < L.num_points; ++v) {
     const uint8_t* rec = pages + (v / L.nodes_per_page) * kPage + (v % L.nodes_per_page) * L.node_size;

@@ -57,6 +57,10 @@ void check_layout(const Layout& L, const PQTables* pq);
 // bytes).  backend: "heap" (fread) or "mmap" (map then copy).
 void read_pages(const std::string& path, int64_t num_pages, const std::string& backend,
                 uint8_t* dst);
+// Pages rank, rank + S, rank + 2S, ... of the page file (one stripe of S),
+// gathered through a read-only mapping so only those pages are touched.
+void read_stripe_pages(const std::string& path, int64_t num_pages, int32_t num_stripes, int32_t rank,
+                       uint8_t* dst);
 
 // Scan every record: degree <= R and neighbour ids < N.  Returns the first
 // offending node or -1.

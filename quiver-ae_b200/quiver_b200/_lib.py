@@ -12,7 +12,8 @@ from . import _build
 
 QV_OK = 0
 QV_UINT8, QV_FLOAT, QV_INT8 = 0, 1, 2
-QV_PAGES_HBM, QV_PAGES_HOST, QV_PAGES_STRIPED = 0, 1, 2
+QV_PAGES_HBM, QV_PAGES_HOST, QV_PAGES_STRIPED, QV_PAGES_SHARED = 0, 1, 2, 3
+QV_STRIPE_HANDLE_BYTES = 64
 QV_EXIT_NONE, QV_EXIT_GPRUNING = 0, 2
 QV_LUT_FP32 = 0
 QV_ADC_AUTO, QV_ADC_THREAD, QV_ADC_PIPE = 0, 1, 2
@@ -38,6 +39,7 @@ class EngineOpts(C.Structure):
         ("index_dir", C.c_char_p), ("data_type", C.c_int32), ("memory_backend", C.c_char_p),
         ("memory_index_file", C.c_char_p), ("device", C.c_int32), ("page_store", C.c_int32),
         ("validate", C.c_int32), ("num_stripes", C.c_int32), ("stripe_devices", C.c_void_p),
+        ("stripe_rank", C.c_int32),
     ]
 
 
@@ -95,6 +97,8 @@ ENGINE_SYMBOLS = {
     "qv_engine_nav_info": (C.c_int, [C.c_void_p, C.POINTER(C.c_int32), C.POINTER(C.c_int32),
                                      C.POINTER(C.c_int32)]),
     "qv_engine_destroy": (None, [C.c_void_p]),
+    "qv_engine_stripe_handle": (C.c_int, [C.c_void_p, C.c_void_p]),
+    "qv_engine_attach_stripes": (C.c_int, [C.c_void_p, C.c_void_p]),
     "qv_search": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int64, C.c_int64, C.POINTER(SearchOpts),
                             C.c_void_p, C.c_void_p, C.c_void_p, C.POINTER(SearchStats)]),
     "qv_search_timed": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int64, C.c_int64, C.POINTER(SearchOpts),

@@ -56,16 +56,21 @@ class Engine:
     @classmethod
     def open(cls, index_dir: str | Path, data_type: str = "uint8", *, memory_backend: str = "heap",
              memory_index_file: str | None = None, device: int = 0, page_store: str = "hbm",
-             validate: bool = False, stripe_devices: list[int] | None = None) -> "Engine":
-        """page_store: "hbm", "host" (pinned mapped DRAM) or "striped" (page p on
-        stripe_devices[p % len(stripe_devices)], read by peer loads)."""
+             validate: bool = False, stripe_devices: list[int] | None = None, num_stripes: int = 0,
+             stripe_rank: int = -1) -> "Engine":
+        """page_store: "hbm", "host" (pinned mapped DRAM), "striped" (page p on
+        stripe_devices[p % len(stripe_devices)], read by peer loads) or "shared"
+        (this process holds stripe `stripe_rank` of `num_stripes`; call
+        stripe_handle / attach_stripes -- shard.open_shared does both -- before
+        searching)."""
         lib = _lib.engine_lib()
         devs = np.ascontiguousarray(stripe_devices or [], dtype=np.int32)
         opts = _lib.EngineOpts(str(index_dir).encode(), _lib.DTYPE_CODES[data_type], memory_backend.encode(),
                                memory_index_file.encode() if memory_index_file else None, device,
                                {"hbm": _lib.QV_PAGES_HBM, "host": _lib.QV_PAGES_HOST,
-                                "striped": _lib.QV_PAGES_STRIPED}[page_store],
-                               1 if validate else 0, len(devs), C.c_void_p(devs.ctypes.data) if len(devs) else None)
+                                "striped": _lib.QV_PAGES_STRIPED, "shared": _lib.QV_PAGES_SHARED}[page_store],
+                               1 if validate else 0, num_stripes if page_store == "shared" else len(devs),
+                               C.c_void_p(devs.ctypes.data) if len(devs) else None, stripe_rank)
         h = C.c_void_p()
         _check(lib.qv_engine_create(C.byref(opts), C.byref(h)))
         return cls(h)
@@ -176,6 +181,19 @@ class Engine:
                                          C.c_void_p(ids.ctypes.data), C.c_void_p(dists.ctypes.data),
                                          C.c_void_p(found.ctypes.data), C.c_void_p(ms.ctypes.data), C.byref(st)))
         return ids, dists, found, ms, st
+
+    def stripe_handle(self) -> bytes:
+        """CUDA IPC handle of the stripe this process holds (shared page store)."""
+        buf = C.create_string_buffer(_lib.QV_STRIPE_HANDLE_BYTES)
+        _check(self._lib.qv_engine_stripe_handle(self._h, buf))
+        return buf.raw
+
+    def attach_stripes(self, handles: list[bytes]) -> None:
+        """Open every other process's stripe (handles in stripe order); the engine can search afterwards."""
+        blob = b"".join(handles)
+        if any(len(h) != _lib.QV_STRIPE_HANDLE_BYTES for h in handles):
+            raise ValueError("every stripe handle is QV_STRIPE_HANDLE_BYTES long")
+        _check(self._lib.qv_engine_attach_stripes(self._h, C.c_char_p(blob)))
 
     def search_stream(self, queries: np.ndarray, params: SearchParams | None = None, *, prefeed: int = -1,
                       admit_min_batch: int = 32, feed_timeout_ms: int = 10000, admit_limit: int = -1):

@@ -49,3 +49,30 @@ def gather_rows(local: np.ndarray, total: int, device=None) -> np.ndarray | None
     if rank != 0:
         return None
     return np.concatenate([parts[r][: strong_rows(r, world, total)[1]].cpu().numpy() for r in range(world)])
+
+
+def exchange_stripe_handles(own: bytes, group=None) -> list[bytes]:
+    """Every rank's stripe handle, in rank order (one all-gather over the process group)."""
+    import torch.distributed as dist
+    world = dist.get_world_size(group)
+    got: list = [None] * world
+    dist.all_gather_object(got, own, group=group)
+    return [bytes(h) for h in got]
+
+
+def open_shared(index_dir, data_type: str, device: int, group=None, **kw):
+    """Open an engine on a page store striped over the ranks of `group`: rank r
+    holds pages p = r (mod world) in its GPU's HBM and reads the others from
+    the ranks that hold them.  World sizes 1, 2, 4 and 8.  Close the engines
+    only after a barrier, since every rank reads every other rank's stripe."""
+    import torch.distributed as dist
+    from .engine import Engine
+    rank, world = dist.get_rank(group), dist.get_world_size(group)
+    eng = Engine.open(index_dir, data_type, device=device, page_store="shared", num_stripes=world,
+                      stripe_rank=rank, **kw)
+    try:
+        eng.attach_stripes(exchange_stripe_handles(eng.stripe_handle(), group))
+    except Exception:
+        eng.close()
+        raise
+    return eng
