@@ -105,3 +105,13 @@ def test_stream_feed_timeout_reports_and_recovers(u8_index):
         sids, sdists, *_ = eng.search_stream(q[:64], p)
     np.testing.assert_array_equal(sids, ids)
     np.testing.assert_array_equal(sdists.view(np.uint32), dists.view(np.uint32))
+
+
+@pytest.mark.gpu
+def test_stream_with_visited_filter_and_nav_off(u8_index):
+    """Modes of the search kernel ride along unchanged: the visited filter under streaming admission."""
+    from quiver_b200 import Engine, SearchParams
+    with Engine.open(u8_index["dir"], "uint8") as eng:
+        _check_stream(eng, _queries(u8_index, 1500),
+                      SearchParams(topk=10, ef_search=48, pipe_width=2, visited_filter=True,
+                                   early_exit_policy="none"), prefeed=0, admit_min_batch=16)
