@@ -226,6 +226,7 @@ Plan make_plan(qv_engine* e, const qv_search_opts& o, int64_t nq) {
     default: qv::bind_search_f32(pl); break;
   }
   CK(cudaFuncSetAttribute(pl.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, e->max_smem_optin));
+  CK(cudaFuncSetAttribute(pl.fn_stream, cudaFuncAttributeMaxDynamicSharedMemorySize, e->max_smem_optin));
 
   const int threads_per_slot = pl.block ? qvk::kBlock : 32;
   auto occupancy = [&](int slots) {
@@ -981,7 +982,7 @@ int qv_search_stream(qv_engine* e, const float* queries, int64_t nq, int64_t dim
     CK(cudaMemcpyAsync(e->d_scratch + 6, e->h_feed, sizeof(int32_t), cudaMemcpyHostToDevice, hs));
     CK(cudaStreamSynchronize(hs));
     int64_t admissions = 1;
-    pl.launch(p, pl.grid, pl.threads, pl.smem, ks);
+    pl.launch_stream(p, pl.grid, pl.threads, pl.smem, ks);
     CK(cudaGetLastError());
 
     // Admission loop (search.cu:983-1051): retire finished copies, charge new

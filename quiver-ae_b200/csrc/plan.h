@@ -20,6 +20,9 @@ struct Plan {
   int threads = 0;      // CTA size
   const void* fn = nullptr;
   void (*launch)(const qvk::SearchParams&, int grid, int block, int smem, cudaStream_t) = nullptr;
+  // the streaming-admission instantiation of the same kernel (waits for each query's feed)
+  const void* fn_stream = nullptr;
+  void (*launch_stream)(const qvk::SearchParams&, int grid, int block, int smem, cudaStream_t) = nullptr;
 };
 
 // Defined in search_u8.cu / search_i8.cu / search_f32.cu: pick the kernel
@@ -28,24 +31,28 @@ void bind_search_u8(Plan& pl);
 void bind_search_i8(Plan& pl);
 void bind_search_f32(Plan& pl);
 
-template <typename T, int MC, int SMAX>
+template <typename T, int MC, int SMAX, bool STREAM>
 void launch_search(const qvk::SearchParams& p, int grid, int block, int smem, cudaStream_t st) {
-  qvk::search_kernel<T, MC, SMAX><<<grid, block, smem, st>>>(p);
+  qvk::search_kernel<T, MC, SMAX, STREAM><<<grid, block, smem, st>>>(p);
 }
 
-template <typename T, int MC, int RP>
+template <typename T, int MC, int RP, bool STREAM>
 void launch_block(const qvk::SearchParams& p, int grid, int block, int smem, cudaStream_t st) {
-  qvk::search_block_kernel<T, MC, RP><<<grid, block, smem, st>>>(p);
+  qvk::search_block_kernel<T, MC, RP, STREAM><<<grid, block, smem, st>>>(p);
 }
 
 template <typename T, int MC, int SMAX>
 void bind_one(Plan& pl) {
   if (pl.block) {
-    pl.fn = reinterpret_cast<const void*>(&qvk::search_block_kernel<T, MC, 32 * SMAX>);
-    pl.launch = &launch_block<T, MC, 32 * SMAX>;
+    pl.fn = reinterpret_cast<const void*>(&qvk::search_block_kernel<T, MC, 32 * SMAX, false>);
+    pl.launch = &launch_block<T, MC, 32 * SMAX, false>;
+    pl.fn_stream = reinterpret_cast<const void*>(&qvk::search_block_kernel<T, MC, 32 * SMAX, true>);
+    pl.launch_stream = &launch_block<T, MC, 32 * SMAX, true>;
   } else {
-    pl.fn = reinterpret_cast<const void*>(&qvk::search_kernel<T, MC, SMAX>);
-    pl.launch = &launch_search<T, MC, SMAX>;
+    pl.fn = reinterpret_cast<const void*>(&qvk::search_kernel<T, MC, SMAX, false>);
+    pl.launch = &launch_search<T, MC, SMAX, false>;
+    pl.fn_stream = reinterpret_cast<const void*>(&qvk::search_kernel<T, MC, SMAX, true>);
+    pl.launch_stream = &launch_search<T, MC, SMAX, true>;
   }
 }
 

@@ -1120,7 +1120,10 @@ __device__ void run_query_block(const SearchParams& p, const BSlot& s, int64_t q
   __syncthreads();
 }
 
-template <typename T, int MC, int RP>
+// STREAM: queries arrive while the kernel runs (streaming admission: wait for
+// each query's feed, publish completions); otherwise every query is present at
+// launch and the loop carries no streaming code.
+template <typename T, int MC, int RP, bool STREAM>
 __global__ void __launch_bounds__(kBlock, 5) search_block_kernel(const SearchParams p) {
   extern __shared__ __align__(16) uint8_t smem[];
   const BSlot s = make_bslot(smem, p.lay);
@@ -1128,7 +1131,8 @@ __global__ void __launch_bounds__(kBlock, 5) search_block_kernel(const SearchPar
   while (true) {
     if (threadIdx.x == 0) {
       int q = atomicAdd(p.work_counter, 1);
-      if (q < p.nq && !wait_fed(p, q)) q = INT32_MAX;
+      if constexpr (STREAM)
+        if (q < p.nq && !wait_fed(p, q)) q = INT32_MAX;
       s.misc[kMiscQid] = q;
     }
     __syncthreads();
@@ -1136,7 +1140,8 @@ __global__ void __launch_bounds__(kBlock, 5) search_block_kernel(const SearchPar
     __syncthreads();
     if (qid >= p.nq) break;
     run_query_block<T, MC, RP>(p, s, qid);
-    if (threadIdx.x == 0) mark_done(p, blockIdx.x, ++done);
+    if constexpr (STREAM)
+      if (threadIdx.x == 0) mark_done(p, blockIdx.x, ++done);
   }
 }
 

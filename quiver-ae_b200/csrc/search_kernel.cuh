@@ -870,7 +870,7 @@ __device__ void run_query(const SearchParams& p, const Slot& s, int64_t qid, int
   __syncwarp();
 }
 
-template <typename T, int MC, int SMAX>
+template <typename T, int MC, int SMAX, bool STREAM>
 __global__ void __launch_bounds__(256) search_kernel(const SearchParams p) {
   extern __shared__ __align__(16) uint8_t smem[];
   const int lane = threadIdx.x & 31;
@@ -882,12 +882,14 @@ __global__ void __launch_bounds__(256) search_kernel(const SearchParams p) {
     int qid = 0;
     if (lane == 0) {
       qid = atomicAdd(p.work_counter, 1);
-      if (qid < p.nq && !wait_fed(p, qid)) qid = INT32_MAX;
+      if constexpr (STREAM)
+        if (qid < p.nq && !wait_fed(p, qid)) qid = INT32_MAX;
     }
     qid = __shfl_sync(kFull, qid, 0);
     if (qid >= p.nq) break;
     run_query<T, MC, SMAX>(p, s, qid, lane);
-    if (lane == 0) mark_done(p, worker, ++done);
+    if constexpr (STREAM)
+      if (lane == 0) mark_done(p, worker, ++done);
   }
 }
 
