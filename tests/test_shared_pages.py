@@ -46,7 +46,7 @@ def _exchange_worker(rank: int, world: int, port: int, out: dict):
 @pytest.mark.parametrize("world", [2, 4])
 def test_stripe_handles_reach_every_rank_in_order(world):
     port = _free_port()
-    with mp.Manager() as m:
+    with mp.get_context("spawn").Manager() as m:  # no fork of a process that may hold a CUDA context
         out = m.dict()
         mp.spawn(_exchange_worker, args=(world, port, out), nprocs=world, join=True)
         for r in range(world):
