@@ -778,6 +778,14 @@ int qv_engine_attach_stripes(qv_engine* e, const void* handles) {
     if (e->attached) fail(QV_ERR_INVALID_ARG, "stripes are already attached");
     CK(cudaSetDevice(e->device));
     const int S = static_cast<int>(e->stripe_ptr.size());
+    // All or nothing: a failure closes the mappings this call opened, so the
+    // engine is left as it was and the call can be retried.
+    std::vector<void*> opened;
+    auto undo = [&] {
+      for (void* p : opened) cudaIpcCloseMemHandle(p);
+      for (int s = 0; s < S; ++s)
+        if (s != e->stripe_rank) e->stripe_ptr[s] = nullptr;
+    };
     for (int s = 0; s < S; ++s) {
       if (s == e->stripe_rank) continue;
       cudaIpcMemHandle_t h;
@@ -785,13 +793,24 @@ int qv_engine_attach_stripes(qv_engine* e, const void* handles) {
                   sizeof(h));
       void* p = nullptr;
       const cudaError_t r = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
-      if (r != cudaSuccess)
+      if (r != cudaSuccess) {
+        undo();
         fail(QV_ERR_CUDA, "opening stripe " + std::to_string(s) + ": " + cudaGetErrorString(r));
-      e->imported.push_back(p);
+      }
+      opened.push_back(p);
       e->stripe_ptr[s] = static_cast<uint8_t*>(p);
     }
-    CK(cudaMalloc(&e->d_stripe_table, sizeof(uint8_t*) * S));
-    CK(cudaMemcpy(e->d_stripe_table, e->stripe_ptr.data(), sizeof(uint8_t*) * S, cudaMemcpyHostToDevice));
+    uint8_t** table = nullptr;
+    cudaError_t r = cudaMalloc(&table, sizeof(uint8_t*) * S);
+    if (r == cudaSuccess)
+      r = cudaMemcpy(table, e->stripe_ptr.data(), sizeof(uint8_t*) * S, cudaMemcpyHostToDevice);
+    if (r != cudaSuccess) {
+      if (table) cudaFree(table);
+      undo();
+      fail(QV_ERR_CUDA, std::string("stripe table: ") + cudaGetErrorString(r));
+    }
+    e->imported.insert(e->imported.end(), opened.begin(), opened.end());
+    e->d_stripe_table = table;
     e->d_pages = e->stripe_ptr[0];
     e->attached = true;
   });
