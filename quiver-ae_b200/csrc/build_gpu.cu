@@ -125,6 +125,7 @@ extern "C" int qv_synth_mixture_gpu(uint64_t seed, int32_t stream, int64_t row0,
     return fail(QV_ERR_INVALID_ARG, "qv_synth_mixture_gpu: invalid argument");
   if (n == 0) return QV_OK;
   if (cudaSetDevice(device) != cudaSuccess) return fail(QV_ERR_CUDA, "qv_synth_mixture_gpu: cannot select device");
+  cudaGetLastError();  // launches below are checked with it: drop an error left by an earlier call
   const std::vector<double> centers = qv_synth::mixture_centers(seed, n_centers, dim, dtype);
   const size_t esize = dtype == QV_UINT8 ? 1 : 4;
   std::string err;
@@ -140,8 +141,10 @@ extern "C" int qv_synth_mixture_gpu(uint64_t seed, int32_t stream, int64_t row0,
     synth_kernel<<<static_cast<unsigned>((cnt + 127) / 128), 128>>>(seed, stream, row0 + s0, cnt,
                                                                      static_cast<int32_t>(dim), n_centers, sigma,
                                                                      dtype, d_c, d_out);
-    const cudaError_t e = cudaMemcpy(static_cast<uint8_t*>(out) + static_cast<size_t>(s0) * dim * esize, d_out,
-                                     static_cast<size_t>(cnt) * dim * esize, cudaMemcpyDeviceToHost);
+    cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess)
+      e = cudaMemcpy(static_cast<uint8_t*>(out) + static_cast<size_t>(s0) * dim * esize, d_out,
+                     static_cast<size_t>(cnt) * dim * esize, cudaMemcpyDeviceToHost);
     if (e != cudaSuccess) return fail(QV_ERR_CUDA, std::string("qv_synth_mixture_gpu: ") + cudaGetErrorString(e));
   }
   return QV_OK;
@@ -163,6 +166,7 @@ extern "C" int qv_pq_encode_gpu(const void* base, int64_t n, int64_t dim, int32_
   if (maxw > kMaxChunkWidth) return fail(QV_ERR_UNSUPPORTED, "qv_pq_encode_gpu: chunk wider than 64 dims");
   if (n == 0) return QV_OK;
   if (cudaSetDevice(device) != cudaSuccess) return fail(QV_ERR_CUDA, "qv_pq_encode_gpu: cannot select device");
+  cudaGetLastError();  // launches below are checked with it: drop an error left by an earlier call
   const size_t esize = dtype == QV_FLOAT ? 4 : 1;
   std::string err;
   DeviceBuffers b;
@@ -173,18 +177,26 @@ extern "C" int qv_pq_encode_gpu(const void* base, int64_t n, int64_t dim, int32_
   void* d_base = b.alloc(static_cast<size_t>(slice) * dim * esize, err);
   uint8_t* d_codes = static_cast<uint8_t*>(b.alloc(static_cast<size_t>(slice) * M, err));
   if (!err.empty()) return fail(QV_ERR_OOM, "qv_pq_encode_gpu: " + err);
-  cudaMemcpy(d_piv, pivots, static_cast<size_t>(256) * dim * 4, cudaMemcpyHostToDevice);
-  cudaMemcpy(d_cen, centroid, static_cast<size_t>(dim) * 4, cudaMemcpyHostToDevice);
-  cudaMemcpy(d_off, chunk_offsets, static_cast<size_t>(M + 1) * 4, cudaMemcpyHostToDevice);
+  // A chunk's 256 centroids sit in shared memory: up to 64 KB, above the 48 KB a launch gets by default.
+  const size_t smem = static_cast<size_t>(256) * maxw * 4;
+  cudaError_t e = cudaFuncSetAttribute(pq_encode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(smem));
+  if (e == cudaSuccess) e = cudaMemcpy(d_piv, pivots, static_cast<size_t>(256) * dim * 4, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMemcpy(d_cen, centroid, static_cast<size_t>(dim) * 4, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMemcpy(d_off, chunk_offsets, static_cast<size_t>(M + 1) * 4, cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) return fail(QV_ERR_CUDA, std::string("qv_pq_encode_gpu: ") + cudaGetErrorString(e));
   for (int64_t s0 = 0; s0 < n; s0 += slice) {
     const int64_t cnt = std::min(slice, n - s0);
-    cudaMemcpy(d_base, static_cast<const uint8_t*>(base) + static_cast<size_t>(s0) * dim * esize,
-               static_cast<size_t>(cnt) * dim * esize, cudaMemcpyHostToDevice);
+    e = cudaMemcpy(d_base, static_cast<const uint8_t*>(base) + static_cast<size_t>(s0) * dim * esize,
+                   static_cast<size_t>(cnt) * dim * esize, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) return fail(QV_ERR_CUDA, std::string("qv_pq_encode_gpu: ") + cudaGetErrorString(e));
     const dim3 grid(static_cast<unsigned>((cnt + 255) / 256), static_cast<unsigned>(M));
-    pq_encode_kernel<<<grid, 256, static_cast<size_t>(256) * maxw * 4>>>(
-        d_base, cnt, static_cast<int32_t>(dim), dtype, d_piv, d_cen, d_off, M, d_codes);
-    const cudaError_t e = cudaMemcpy(codes + static_cast<size_t>(s0) * M, d_codes, static_cast<size_t>(cnt) * M,
-                                     cudaMemcpyDeviceToHost);
+    pq_encode_kernel<<<grid, 256, smem>>>(d_base, cnt, static_cast<int32_t>(dim), dtype, d_piv, d_cen, d_off, M,
+                                          d_codes);
+    e = cudaGetLastError();
+    if (e == cudaSuccess)
+      e = cudaMemcpy(codes + static_cast<size_t>(s0) * M, d_codes, static_cast<size_t>(cnt) * M,
+                     cudaMemcpyDeviceToHost);
     if (e != cudaSuccess) return fail(QV_ERR_CUDA, std::string("qv_pq_encode_gpu: ") + cudaGetErrorString(e));
   }
   return QV_OK;

@@ -616,13 +616,13 @@ int run_vamana(const T* h_data, int64_t n, int32_t dim, int32_t R, int32_t L, fl
       }
       const int64_t total = cnt * R;
       install_kernel<<<static_cast<unsigned>((total + 255) / 256), 256>>>(a, start, cnt, keys);
-      cub::DeviceRadixSort::SortKeys(sort_tmp, sort_bytes, keys, keys2, static_cast<int>(total));
+      ck(cub::DeviceRadixSort::SortKeys(sort_tmp, sort_bytes, keys, keys2, static_cast<int>(total)), "sort");
       ck(cudaMemsetAsync(nheads, 0, 16), "memset");
       heads_kernel<<<static_cast<unsigned>((total + 255) / 256), 256>>>(keys2, total, heads, nheads);
       int32_t nh[3] = {0, 0, 0};
       ck(cudaMemcpy(nh, nheads, 12, cudaMemcpyDeviceToHost), "group count");
       if (nh[0] > 0) {
-        cub::DeviceRadixSort::SortKeys(sort_tmp, hsort_bytes, heads, heads2, nh[0]);
+        ck(cub::DeviceRadixSort::SortKeys(sort_tmp, hsort_bytes, heads, heads2, nh[0]), "sort");
         longest_kernel<<<static_cast<unsigned>((nh[0] + 255) / 256), 256>>>(heads2, nheads);
         ck(cudaMemcpy(nh, nheads, 12, cudaMemcpyDeviceToHost), "longest group");
         const int64_t per_warp = 2 * (static_cast<int64_t>(R) + nh[2]);
@@ -649,6 +649,7 @@ int run_vamana(const T* h_data, int64_t n, int32_t dim, int32_t R, int32_t L, fl
         reverse_kernel<T><<<static_cast<unsigned>(warps / kWarps), kWarps * 32>>>(a, r, alpha);
       }
       int32_t e[2] = {0, 0};
+      ck(cudaGetLastError(), "build kernel launch");  // a refused launch leaves the error words clear
       ck(cudaMemcpy(e, a.err, 8, cudaMemcpyDeviceToHost), "build kernels");
       if (e[0] != kBuildOk && err.empty())
         err = e[0] == kErrExpansions ? "a greedy search expanded more than " + std::to_string(kExpCap) +
@@ -686,6 +687,7 @@ extern "C" int qv_vamana_gpu(const void* base, int64_t n, int64_t dim, int32_t d
     qv::set_last_error("qv_vamana_gpu: cannot select device " + std::to_string(device));
     return QV_ERR_CUDA;
   }
+  cudaGetLastError();  // launches are checked with it: drop an error left by an earlier call
   std::string err;
   int rc;
   if (dtype == QV_UINT8)

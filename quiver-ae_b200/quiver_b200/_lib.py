@@ -11,9 +11,12 @@ from pathlib import Path
 from . import _build
 
 QV_OK = 0
+(QV_ERR_INVALID_ARG, QV_ERR_IO, QV_ERR_BAD_INDEX, QV_ERR_CUDA, QV_ERR_DEVICE, QV_ERR_UNSUPPORTED,
+ QV_ERR_OOM) = range(1, 8)
 QV_UINT8, QV_FLOAT, QV_INT8 = 0, 1, 2
 QV_PAGES_HBM, QV_PAGES_HOST, QV_PAGES_STRIPED, QV_PAGES_SHARED = 0, 1, 2, 3
 QV_STRIPE_HANDLE_BYTES = 64
+QV_NOALLOC_SCRATCH_BYTES = 4 << 20
 QV_EXIT_NONE, QV_EXIT_GPRUNING = 0, 2
 QV_LUT_FP32 = 0
 QV_ADC_AUTO, QV_ADC_THREAD, QV_ADC_PIPE = 0, 1, 2

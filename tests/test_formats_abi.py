@@ -49,6 +49,17 @@ def test_python_binding_covers_the_header(engine_lib):
     assert declared == set(_lib.ENGINE_SYMBOLS)
 
 
+def test_python_constants_match_the_header():
+    """Every integer #define of the C header has the same value in the Python binding."""
+    from quiver_b200 import _lib
+    text = (REPO / "include" / "quiver_b200.h").read_text()
+    defines = re.findall(r"^#define (QV_[A-Z0-9_]+) \(?(\d+)u?(?: << (\d+))?\)?", text, re.M)
+    assert len(defines) >= 20
+    for name, value, shift in defines:
+        expected = int(value) << int(shift or 0)
+        assert getattr(_lib, name, None) == expected, f"{name}: header {expected}, binding {getattr(_lib, name, None)}"
+
+
 def test_library_loads_without_gpu(engine_lib):
     assert engine_lib.qv_version().decode().startswith("quiver-b200")
 

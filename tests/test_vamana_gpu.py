@@ -26,6 +26,28 @@ def test_vamana_gpu_argument_checks_without_gpu():
     assert b"R <=" in lib.qv_last_error()
 
 
+def test_pq_encode_gpu_argument_checks_without_gpu():
+    """Chunk offsets are checked before any device call; chunks wider than 64 dims are refused."""
+    import ctypes as C
+    from quiver_b200 import _lib
+    lib = _lib.engine_lib()
+    base = np.zeros((4, 130), dtype=np.uint8)
+    piv = np.zeros((256, 130), dtype=np.float32)
+    cen = np.zeros(130, dtype=np.float32)
+    codes = np.zeros((4, 2), dtype=np.uint8)
+
+    def call(offs):
+        offs = np.asarray(offs, dtype=np.int32)
+        return lib.qv_pq_encode_gpu(base.ctypes.data, 4, 130, _lib.QV_UINT8, len(offs) - 1, piv.ctypes.data,
+                                    cen.ctypes.data, offs.ctypes.data, 0, codes.ctypes.data)
+    assert call([0, 65, 130]) == _lib.QV_ERR_UNSUPPORTED
+    assert b"wider than 64" in lib.qv_last_error()
+    assert call([0, 70, 60]) == _lib.QV_ERR_INVALID_ARG
+    assert b"chunk offsets" in lib.qv_last_error()
+    assert call([0, 64, 131]) == _lib.QV_ERR_INVALID_ARG
+    assert lib.qv_pq_encode_gpu(None, 4, 130, _lib.QV_UINT8, 2, None, None, None, 0, None) == _lib.QV_ERR_INVALID_ARG
+
+
 CASES = [
     # (dtype, n, dim, centers, sigma, R, L, seed)
     ("uint8", 6000, 64, 12, 20.0, 32, 48, 3),
@@ -92,8 +114,10 @@ def test_gpu_synth_equals_host(dtype, dim, sigma):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("dtype,dim,M", [("uint8", 128, 32), ("float", 96, 32), ("uint8", 50, 12)])
+@pytest.mark.parametrize("dtype,dim,M", [("uint8", 128, 32), ("float", 96, 32), ("uint8", 50, 12),
+                                         ("uint8", 128, 2), ("float", 104, 2)])  # 64- and 52-dim chunks
 def test_gpu_pq_encode_equals_host(dtype, dim, M):
+    """Chunks wider than 48 dims stage more than the default 48 KB of shared memory per block."""
     from quiver_b200 import builder
     base = builder.synth_mixture(8, 20000, dim, 40, 20.0 if dtype == "uint8" else 0.1, dtype)
     piv, cen, offs = builder.pq_train(base, M, sample=5000, iters=4, seed=1)
