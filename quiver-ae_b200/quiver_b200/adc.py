@@ -53,11 +53,18 @@ def adc_batch(codes, luts, ids=None, first=None, n_per_query: int | None = None,
     luts = luts.contiguous()
     if out is None:
         out = torch.empty((nq, n), dtype=torch.float32, device=codes.device)
-    elif out.dtype != torch.float32 or out.numel() != nq * n or not out.is_contiguous():
-        raise ValueError("out must be a contiguous float32 tensor of nq * n elements")
+    elif (out.dtype != torch.float32 or out.numel() != nq * n or not out.is_contiguous()
+          or out.device != codes.device):
+        raise ValueError("out must be a contiguous float32 tensor of nq * n elements on the codes' device")
     st = stream if stream is not None else torch.cuda.current_stream(codes.device)
-    _check(_lib.engine_lib().qv_adc_batch(
-        C.c_void_p(codes.data_ptr()), num_points, M, C.c_void_p(luts.data_ptr()), nq,
-        C.c_void_p(ids.data_ptr()) if ids is not None else None, first_ptr, n,
-        C.c_void_p(out.data_ptr()), KERNELS[kernel], C.c_void_p(st.cuda_stream)))
+    if stream is not None:
+        # the inputs (or their contiguous copies) stay allocated until the kernel on `stream` has read them
+        for t in (codes, luts, ids, first, out):
+            if t is not None:
+                t.record_stream(stream)
+    with torch.cuda.device(codes.device):  # the launch goes to the current device
+        _check(_lib.engine_lib().qv_adc_batch(
+            C.c_void_p(codes.data_ptr()), num_points, M, C.c_void_p(luts.data_ptr()), nq,
+            C.c_void_p(ids.data_ptr()) if ids is not None else None, first_ptr, n,
+            C.c_void_p(out.data_ptr()), KERNELS[kernel], C.c_void_p(st.cuda_stream)))
     return out

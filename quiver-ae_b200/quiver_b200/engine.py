@@ -49,9 +49,12 @@ class SearchParams:
 class Engine:
     """One index resident on one GPU."""
 
-    def __init__(self, handle: C.c_void_p):
+    def __init__(self, handle: C.c_void_p, device: int = 0):
         self._h = handle
         self._lib = _lib.engine_lib()
+        self.device = device  # the GPU the engine's kernels run on
+        i = self.info
+        self._dim, self._M = int(i.dim), int(i.num_chunks)
 
     @classmethod
     def open(cls, index_dir: str | Path, data_type: str = "uint8", *, memory_backend: str = "heap",
@@ -73,7 +76,7 @@ class Engine:
                                C.c_void_p(devs.ctypes.data) if len(devs) else None, stripe_rank)
         h = C.c_void_p()
         _check(lib.qv_engine_create(C.byref(opts), C.byref(h)))
-        return cls(h)
+        return cls(h, device)
 
     @classmethod
     def from_arrays(cls, *, data_type: str, num_points: int, dim: int, node_size: int, nodes_per_page: int,
@@ -90,7 +93,7 @@ class Engine:
         _check(lib.qv_engine_create_from_arrays(C.byref(arr), device,
                                                 {"hbm": _lib.QV_PAGES_HBM, "host": _lib.QV_PAGES_HOST}[page_store],
                                                 C.byref(h)))
-        return cls(h)
+        return cls(h, device)
 
     def close(self) -> None:
         if self._h:
@@ -239,37 +242,94 @@ class Engine:
         _check(self._lib.qv_search(self._h, C.c_void_p(q_ptr), nq, dim, C.byref(o), C.c_void_p(ids_ptr),
                                    C.c_void_p(dists_ptr), C.c_void_p(found_ptr) if found_ptr else None, None))
 
+    def _arg(self, t, name: str, dtype, numel: int | None = None):
+        """Device pointer of a contiguous CUDA tensor on the engine's GPU, after checking its type and size."""
+        import torch
+        if t is None:
+            return None
+        if not isinstance(t, torch.Tensor) or not t.is_cuda or t.device.index != self.device:
+            raise ValueError(f"{name} must be a CUDA tensor on cuda:{self.device}")
+        if t.dtype != dtype:
+            raise ValueError(f"{name} must be {dtype}, got {t.dtype}")
+        if not t.is_contiguous():
+            raise ValueError(f"{name} must be contiguous")
+        if numel is not None and t.numel() != numel:
+            raise ValueError(f"{name} must hold {numel} elements, got {t.numel()}")
+        return C.c_void_p(t.data_ptr())
+
+    def _queries(self, t, name: str) -> int:
+        if t.dim() != 2 or t.shape[1] != self._dim:
+            raise ValueError(f"{name} must be [nq, {self._dim}]")
+        return t.shape[0]
+
     def search_device(self, d_queries, params: SearchParams, d_ids, d_dists, d_found=None, d_steps=None,
                       d_nbrs=None, stream=None) -> None:
-        """Enqueue a search on CUDA tensors (torch) without synchronising."""
+        """Enqueue a search on CUDA tensors (torch) without synchronising.
+
+        d_queries float32 [nq, dim]; d_ids int32 and d_dists float32 [nq, topk];
+        d_found, d_steps int32 [nq] and d_nbrs int64 [nq] optional.  stream: a
+        cudaStream_t handle, 0 for the legacy default stream, or None for
+        torch's current stream on the engine's GPU.
+        """
+        import torch
+        f32, i32 = torch.float32, torch.int32
+        nq = self._queries(d_queries, "d_queries")
+        k = params.topk
+        args = (self._arg(d_queries, "d_queries", f32), self._arg(d_ids, "d_ids", i32, nq * k),
+                self._arg(d_dists, "d_dists", f32, nq * k), self._arg(d_found, "d_found", i32, nq),
+                self._arg(d_steps, "d_steps", i32, nq), self._arg(d_nbrs, "d_nbrs", torch.int64, nq))
+        if stream is None:
+            stream = torch.cuda.current_stream(self.device).cuda_stream
         o = params.to_c()
-
-        def ptr(t):
-            return C.c_void_p(t.data_ptr()) if t is not None else None
-
-        # None: the engine's own stream; 0: the legacy default stream
-        # (cudaStreamLegacy, handle 0x1); anything else: that cudaStream_t.
-        st = None if stream is None else C.c_void_p(1 if stream == 0 else stream)
-        _check(self._lib.qv_search_device(self._h, ptr(d_queries), d_queries.shape[0], C.byref(o), ptr(d_ids),
-                                          ptr(d_dists), ptr(d_found), ptr(d_steps), ptr(d_nbrs), st))
+        # 0 is the legacy default stream (cudaStreamLegacy, handle 0x1); a null handle would select the
+        # engine's own stream, which is not ordered after torch's work.
+        st = C.c_void_p(1 if stream == 0 else stream)
+        _check(self._lib.qv_search_device(self._h, args[0], nq, C.byref(o), *args[1:], st))
 
     def check_device_status(self) -> None:
         _check(self._lib.qv_check_device_status(self._h))
 
     # component kernels (torch CUDA tensors) -------------------------------
+    # The component calls run on the engine's own stream and return when their kernel has finished; torch's
+    # current stream is drained first, so inputs that torch kernels produced are complete.
+    def _drain_torch(self) -> None:
+        import torch
+        torch.cuda.current_stream(self.device).synchronize()
+
     def build_lut(self, d_queries, d_lut, d_q2) -> None:
-        _check(self._lib.qv_build_lut_device(self._h, C.c_void_p(d_queries.data_ptr()), d_queries.shape[0],
-                                             C.c_void_p(d_lut.data_ptr()), C.c_void_p(d_q2.data_ptr()), None))
+        """d_queries float32 [nq, dim] -> d_lut float32 [nq, M, 256] and q'' d_q2 float32 [nq, dim]."""
+        import torch
+        nq = self._queries(d_queries, "d_queries")
+        args = (self._arg(d_queries, "d_queries", torch.float32),
+                self._arg(d_lut, "d_lut", torch.float32, nq * self._M * 256),
+                self._arg(d_q2, "d_q2", torch.float32, nq * self._dim))
+        self._drain_torch()
+        _check(self._lib.qv_build_lut_device(self._h, args[0], nq, args[1], args[2], None))
+
+    def _pairs(self, d_query_of, d_ids, d_out):
+        import torch
+        n = d_ids.numel()
+        return n, (self._arg(d_query_of, "d_query_of", torch.int32, n), self._arg(d_ids, "d_ids", torch.int32),
+                   self._arg(d_out, "d_out", torch.float32, n))
 
     def adc(self, d_lut, d_query_of, d_ids, d_out) -> None:
-        _check(self._lib.qv_adc_device(self._h, C.c_void_p(d_lut.data_ptr()), C.c_void_p(d_query_of.data_ptr()),
-                                       C.c_void_p(d_ids.data_ptr()), d_ids.shape[0], C.c_void_p(d_out.data_ptr()),
-                                       None))
+        """d_out[i] = ADC of code d_ids[i] under LUT d_lut[d_query_of[i]] (d_lut float32 [nq, M, 256])."""
+        import torch
+        lut = self._arg(d_lut, "d_lut", torch.float32)
+        if d_lut.numel() % (self._M * 256) != 0:
+            raise ValueError(f"d_lut must be float32 [nq, {self._M}, 256]")
+        n, (qof, ids, out) = self._pairs(d_query_of, d_ids, d_out)
+        self._drain_torch()
+        _check(self._lib.qv_adc_device(self._h, lut, qof, ids, n, out, None))
 
     def exact_l2(self, d_q2, d_query_of, d_ids, d_out) -> None:
-        _check(self._lib.qv_exact_l2_device(self._h, C.c_void_p(d_q2.data_ptr()), C.c_void_p(d_query_of.data_ptr()),
-                                            C.c_void_p(d_ids.data_ptr()), d_ids.shape[0],
-                                            C.c_void_p(d_out.data_ptr()), None))
+        """d_out[i] = exact squared L2 of q'' d_q2[d_query_of[i]] (float32 [nq, dim]) and node d_ids[i]."""
+        import torch
+        self._queries(d_q2, "d_q2")
+        q2 = self._arg(d_q2, "d_q2", torch.float32)
+        n, (qof, ids, out) = self._pairs(d_query_of, d_ids, d_out)
+        self._drain_torch()
+        _check(self._lib.qv_exact_l2_device(self._h, q2, qof, ids, n, out, None))
 
 
 def open_index_arrays(index_dir: str | Path, data_type: str) -> dict:

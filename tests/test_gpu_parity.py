@@ -132,3 +132,42 @@ def test_host_page_store_parity(u8_index):
         b = ed.search(u8_index["queries"], p)
     for x, y in zip(a, b):
         np.testing.assert_array_equal(x, y)
+
+
+def test_search_device_on_torch_streams(engines, u8_index):
+    """search_device on CUDA tensors -- on torch's current stream by default (here the legacy default
+    stream), or on a stream given -- returns qv_search's results; tensors of the wrong type, layout or size
+    are refused before the launch."""
+    import torch
+    from quiver_b200 import SearchParams
+    eng = engines["u8"]
+    q = u8_index["queries"][:64]
+    p = SearchParams(ef_search=45, pipe_width=2, early_exit_policy="none")
+    ids_h, d_h, f_h = eng.search(q, p)
+    dq = torch.from_numpy(q).cuda() * 1.0  # written by a torch kernel on the current stream
+    nq, k = q.shape[0], p.topk
+    for stream in (None, torch.cuda.Stream()):
+        d_ids = torch.full((nq, k), -7, dtype=torch.int32, device="cuda")
+        d_dists = torch.empty((nq, k), dtype=torch.float32, device="cuda")
+        d_found = torch.empty(nq, dtype=torch.int32, device="cuda")
+        if stream is None:
+            eng.search_device(dq, p, d_ids, d_dists, d_found)
+        else:
+            stream.wait_stream(torch.cuda.current_stream())
+            eng.search_device(dq, p, d_ids, d_dists, d_found, stream=stream.cuda_stream)
+        torch.cuda.synchronize()
+        eng.check_device_status()
+        np.testing.assert_array_equal(d_ids.cpu().numpy(), ids_h)
+        np.testing.assert_array_equal(d_dists.cpu().numpy().view(np.uint32), d_h.view(np.uint32))
+        np.testing.assert_array_equal(d_found.cpu().numpy(), f_h)
+    with pytest.raises(ValueError, match="torch.int32"):
+        eng.search_device(dq, p, d_ids.float(), d_dists)
+    with pytest.raises(ValueError, match="contiguous"):
+        eng.search_device(dq, p, d_ids.t(), d_dists)
+    with pytest.raises(ValueError, match="elements"):
+        eng.search_device(dq, p, d_ids[:-1], d_dists)
+    with pytest.raises(ValueError, match="elements"):
+        eng.build_lut(dq, torch.empty((nq, 31, 256), device="cuda"), torch.empty_like(dq))
+    with pytest.raises(ValueError, match="elements"):
+        eng.exact_l2(dq, torch.zeros(4, dtype=torch.int32, device="cuda"),
+                     torch.zeros(5, dtype=torch.int32, device="cuda"), torch.empty(5, device="cuda"))

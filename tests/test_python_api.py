@@ -171,3 +171,51 @@ def test_cli_reports_missing_index(cli, index_dir, tmp_path):
     q.write_bytes(struct.pack("<ii", 1, 4) + np.ones(4, np.float32).tobytes())
     r = _run(cli, "--index-dir", index_dir, "--query", q, "--data-type", "float")
     assert r.returncode == 1 and "No *_disk.index or disk.index found" in r.stderr
+
+
+def _bare_engine(device=0, dim=8, M=2):
+    """An Engine object with no library handle: only the Python-side argument checks can run on it."""
+    from quiver_b200 import Engine
+    e = Engine.__new__(Engine)
+    e._h, e.device, e._dim, e._M = None, device, dim, M
+    return e
+
+
+def test_tensor_methods_refuse_bad_tensors_before_any_device_call():
+    import torch
+    from quiver_b200 import SearchParams
+    e = _bare_engine()
+    p = SearchParams(topk=3)
+    cpu_q = torch.zeros((5, 8), dtype=torch.float32)
+    with pytest.raises(ValueError, match="CUDA tensor on cuda:0"):
+        e.search_device(cpu_q, p, torch.zeros((5, 3), dtype=torch.int32), torch.zeros((5, 3)))
+    with pytest.raises(ValueError, match=r"\[nq, 8\]"):
+        e.search_device(torch.zeros((5, 7)), p, None, None)
+    with pytest.raises(ValueError, match=r"\[nq, 8\]"):
+        e.build_lut(torch.zeros(40), None, None)
+    with pytest.raises(ValueError, match="CUDA tensor"):
+        e.exact_l2(cpu_q, torch.zeros(4, dtype=torch.int32), torch.zeros(4, dtype=torch.int32), torch.zeros(4))
+    with pytest.raises(ValueError, match="CUDA tensor"):
+        e.adc(torch.zeros((5, 2, 256)), torch.zeros(4, dtype=torch.int32), torch.zeros(4, dtype=torch.int32),
+              torch.zeros(4))
+
+
+def test_tensor_argument_check_messages():
+    """dtype, contiguity and size are checked in that order once the tensor is on the engine's GPU; on a
+    host without a GPU the device check comes first."""
+    import torch
+    e = _bare_engine()
+    t = torch.zeros(6, dtype=torch.float32)
+    assert e._arg(None, "x", torch.float32) is None
+    with pytest.raises(ValueError, match="x must be a CUDA tensor on cuda:0"):
+        e._arg(t, "x", torch.float32, 6)
+    with pytest.raises(ValueError, match="must be a CUDA tensor"):
+        e._arg(t.numpy(), "x", torch.float32)
+
+
+def test_adc_batch_refuses_host_tensors():
+    import torch
+    from quiver_b200.adc import adc_batch
+    with pytest.raises(ValueError, match="codes must be a CUDA uint8"):
+        adc_batch(torch.zeros((10, 32), dtype=torch.uint8), torch.zeros((1, 32, 256)),
+                  torch.zeros((1, 4), dtype=torch.int32))
