@@ -86,7 +86,7 @@ typedef struct {
   const char* memory_backend;     /* "heap" or "mmap": how the page file is read (memory_backend.hpp:7-20) */
   const char* memory_index_file;  /* NULL or "" -> the discovered *_disk.index */
   int32_t device;                 /* CUDA ordinal */
-  int32_t page_store;             /* QV_PAGES_HBM or QV_PAGES_HOST */
+  int32_t page_store;             /* QV_PAGES_HBM / _HOST / _STRIPED / _SHARED (see above) */
   int32_t validate;               /* 1: check every adjacency list at load (degree <= R, ids < N) */
   int32_t num_stripes;            /* QV_PAGES_STRIPED: S, a power of two <= 8 */
   const int32_t* stripe_devices;  /* QV_PAGES_STRIPED: [S] CUDA ordinals (repeats allowed); every one

@@ -79,3 +79,44 @@ def test_c_program_links_and_calls_the_abi(tmp_path, libs, u8_index):
     assert run.returncode == 0, (run.returncode, run.stderr)
     n, dim, R, M = map(int, run.stdout.split())
     assert (n, dim, R, M) == (u8_index["base"].shape[0], u8_index["base"].shape[1], 64, 32)
+
+
+SIZES = r"""
+#include <stdio.h>
+#include "quiver_b200.h"
+int main(void) {
+  printf("qv_index_info %zu\n", sizeof(qv_index_info));
+  printf("qv_engine_opts %zu\n", sizeof(qv_engine_opts));
+  printf("qv_index_arrays %zu\n", sizeof(qv_index_arrays));
+  printf("qv_search_opts %zu\n", sizeof(qv_search_opts));
+  printf("qv_search_stats %zu\n", sizeof(qv_search_stats));
+  printf("qv_stream_opts %zu\n", sizeof(qv_stream_opts));
+  printf("qv_stream_stats %zu\n", sizeof(qv_stream_stats));
+  return 0;
+}
+"""
+
+
+def test_python_structures_have_the_c_sizes(tmp_path):
+    """Every ctypes mirror of a header struct has the size the C compiler gives it, so no field was added
+    on one side only."""
+    import ctypes as C
+    from quiver_b200 import _lib
+    gcc = shutil.which("gcc")
+    if gcc is None:
+        pytest.skip("no C compiler")
+    src = tmp_path / "sizes.c"
+    src.write_text(SIZES)
+    exe = tmp_path / "sizes"
+    res = subprocess.run([gcc, "-std=c99", "-Wall", "-Werror", "-I", str(REPO / "include"), str(src), "-o",
+                          str(exe)], capture_output=True, text=True)
+    assert res.returncode == 0, res.stderr
+    sizes = dict(line.split() for line in subprocess.run([str(exe)], capture_output=True, text=True,
+                                                          check=True).stdout.splitlines())
+    mirror = {"qv_index_info": _lib.IndexInfo, "qv_engine_opts": _lib.EngineOpts,
+              "qv_index_arrays": _lib.IndexArrays, "qv_search_opts": _lib.SearchOpts,
+              "qv_search_stats": _lib.SearchStats, "qv_stream_opts": _lib.StreamOpts,
+              "qv_stream_stats": _lib.StreamStats}
+    assert set(sizes) == set(mirror)
+    for name, cls in mirror.items():
+        assert C.sizeof(cls) == int(sizes[name]), f"{name}: C {sizes[name]} bytes, ctypes {C.sizeof(cls)}"
