@@ -295,6 +295,9 @@ def main() -> int:
                     help="also time small batches end to end, e.g. 1,4,16 (latency mode; rank 0 only)")
     ap.add_argument("--stripe-devices", default="",
                     help="stripe the page store over these GPUs, e.g. 0,1 (pages p mod S; peer loads)")
+    ap.add_argument("--page-store", default="hbm", choices=["hbm", "host"],
+                    help="where the node records live: the search GPU's HBM, or pinned host DRAM mapped into the "
+                         "GPU's address space and read over PCIe")
     ap.add_argument("--stripe-shared", action="store_true",
                     help="under torchrun: rank r holds pages p = r (mod N) and reads the rest from the other "
                          "ranks' GPUs (CUDA IPC, peer loads)")
@@ -361,7 +364,7 @@ def main() -> int:
     elif stripes:
         eng = Engine.open(d, w.data_type, device=local, page_store="striped", stripe_devices=stripes)
     else:
-        eng = Engine.open(d, w.data_type, device=local)
+        eng = Engine.open(d, w.data_type, device=local, page_store=args.page_store)
     nav_nodes = eng.nav_info[0] if args.nav else 0
 
     # ef calibration on the first CALIB_QUERIES rows (identical on every rank)
@@ -494,6 +497,7 @@ def main() -> int:
                        "page_store": (f"shared: rank r holds pages p = r mod {world}, the rest read from the other "
                                       f"ranks' GPUs (CUDA IPC peer loads)" if args.stripe_shared
                                       else f"striped over GPUs {stripes} (peer loads)" if stripes
+                                      else "pinned host DRAM, mapped (PCIe loads)" if args.page_store == "host"
                                       else "HBM of the search GPU")},
             "recall_at_10": recall,
             "p50_ms": streaming["p50_ms"] if streaming else p50,
@@ -513,6 +517,11 @@ def main() -> int:
             "gpu_launches": args.steps,
             "clocks": clocks,
         }
+        if args.page_store == "host" and not stripes and not args.stripe_shared:
+            # the committed capture is of the HBM page store; here the records come over PCIe
+            line["roofline"]["traffic"] = None
+            line["roofline"]["note"] = (f"node records ({expansions * info.node_size / 1e9:.2f} GB per launch) are read "
+                                        "from pinned host DRAM over PCIe; the HBM fraction does not bound this mode")
         if latency:
             line["latency_mode"] = {"per_batch_size": latency,
                                     "how": "qv_search on pinned host buffers, host wall time per batch "
