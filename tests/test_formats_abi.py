@@ -157,3 +157,65 @@ def test_plain_read_errors_do_not_touch_cuda(engine_lib):
     opts = _lib.EngineOpts(b"/nonexistent", 7, b"heap", None, 0, 0, 0)
     h = C.c_void_p()
     assert engine_lib.qv_engine_create(C.byref(opts), C.byref(h)) == 1
+
+
+@pytest.mark.parametrize("seed", range(12))
+def test_sliced_page_writer_equals_whole_build(tmp_path, engine_lib, seed):
+    """write_disk_index writes its pages a slice of nodes at a time; for any slice size (forcing partial last
+    pages and slice boundaries inside the data) the file equals the whole-array page build, every record
+    reads back (vector, degree, the first `degree` ids, zeros after), and the C++ reader agrees on the
+    header."""
+    from quiver_b200 import _lib, formats
+    rng = np.random.default_rng(seed)
+    dtype = [np.uint8, np.int8, np.float32][seed % 3]
+    dim = int(rng.integers(3, 140))
+    R = int(rng.integers(1, 70))
+    elem = np.dtype(dtype).itemsize
+    if seed % 2 == 0:
+        dim = max(4, dim - dim % 4)  # whole 32-bit words: an index the engine loads
+    if dim * elem + 4 * (R + 1) > 4096:
+        dim = (4096 - 4 * (R + 1)) // elem
+    n = int(rng.integers(1, 400))
+    if dtype == np.float32:
+        data = rng.standard_normal((n, dim)).astype(np.float32)
+    else:
+        lim = np.iinfo(dtype)
+        data = rng.integers(lim.min, lim.max + 1, size=(n, dim)).astype(dtype)
+    degree = rng.integers(0, R + 1, size=n).astype(np.int32)
+    graph = np.full((n, R), -1, dtype=np.int32)
+    for v in range(n):
+        graph[v, :degree[v]] = rng.integers(0, n, size=degree[v])
+    medoid = int(rng.integers(0, n))
+    d = tmp_path / "ix"
+    d.mkdir()
+    lay = formats.write_disk_index(d / "ann_disk.index", data, graph, degree, medoid, R,
+                                   nodes_per_slice=int(rng.integers(1, 60)))
+    whole, node_size, npp = formats.build_pages(data, graph, degree, R)
+    assert (lay.node_size, lay.nodes_per_page, lay.num_pages) == (node_size, npp, whole.shape[0])
+    assert (d / "ann_disk.index").stat().st_size == 4096 * (lay.num_pages + 1)
+    pages = formats.read_pages(d / "ann_disk.index", lay.num_pages)
+    np.testing.assert_array_equal(pages, whole)
+    dsize = dim * elem
+    for v in range(n):
+        rec = pages[v // npp, (v % npp) * node_size:(v % npp + 1) * node_size]
+        np.testing.assert_array_equal(rec[:dsize].view(dtype), data[v])
+        deg = int(rec[dsize:dsize + 4].view("<u4")[0])
+        assert deg == degree[v]
+        ids = rec[dsize + 4:].view("<u4")
+        np.testing.assert_array_equal(ids[:deg], graph[v, :deg])
+        assert not ids[deg:].any()
+    dt_name = {np.uint8: "uint8", np.int8: "int8", np.float32: "float"}[dtype]
+    hdr = formats.read_disk_index_header(d / "ann_disk.index", dt_name)
+    assert (hdr.num_points, hdr.dim, hdr.medoid, hdr.max_degree) == (n, dim, medoid, R)
+    M = 1
+    formats.write_pq(d / "ann", np.zeros((256, dim), np.float32), np.zeros(dim, np.float32),
+                     np.array([0, dim], np.int32), np.zeros((n, M), np.uint8))
+    rc, info, msg = _probe(engine_lib, d, dt_name)
+    if dsize % 4:
+        # the ids after the vector are 32-bit words: a record whose vector is not a whole number of words
+        # would put them off alignment, so the engine refuses the index rather than load it
+        assert rc == _lib.QV_ERR_BAD_INDEX and "4-byte aligned" in msg
+        return
+    assert rc == 0, msg
+    assert (info.num_points, info.dim, info.max_degree, info.node_size, info.nodes_per_page, info.num_pages,
+            info.medoid) == (n, dim, R, node_size, npp, lay.num_pages, medoid)
