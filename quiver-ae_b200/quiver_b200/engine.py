@@ -258,7 +258,8 @@ class Engine:
         return C.c_void_p(t.data_ptr())
 
     def _queries(self, t, name: str) -> int:
-        if t.dim() != 2 or t.shape[1] != self._dim:
+        import torch
+        if not isinstance(t, torch.Tensor) or t.dim() != 2 or t.shape[1] != self._dim:
             raise ValueError(f"{name} must be [nq, {self._dim}]")
         return t.shape[0]
 

@@ -193,6 +193,8 @@ def test_tensor_methods_refuse_bad_tensors_before_any_device_call():
         e.search_device(torch.zeros((5, 7)), p, None, None)
     with pytest.raises(ValueError, match=r"\[nq, 8\]"):
         e.build_lut(torch.zeros(40), None, None)
+    with pytest.raises(ValueError, match=r"\[nq, 8\]"):
+        e.search_device(np.zeros((5, 8), np.float32), p, None, None)  # a host array, not a tensor
     with pytest.raises(ValueError, match="CUDA tensor"):
         e.exact_l2(cpu_q, torch.zeros(4, dtype=torch.int32), torch.zeros(4, dtype=torch.int32), torch.zeros(4))
     with pytest.raises(ValueError, match="CUDA tensor"):
