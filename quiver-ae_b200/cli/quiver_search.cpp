@@ -155,10 +155,22 @@ std::vector<T> read_typed_bin(const std::string& path, size_t& dims, size_t& cou
   int32_t n = 0, d = 0;
   in.read(reinterpret_cast<char*>(&n), 4);
   in.read(reinterpret_cast<char*>(&d), 4);
+  // The reference reads on regardless; a short or malformed file would leave the search
+  // uninitialised queries, so it is refused here.
+  if (!in || n < 0 || d < 0) {
+    std::cerr << "Invalid header in file " << path << std::endl;
+    std::exit(1);
+  }
   dims = static_cast<size_t>(d);
   count = static_cast<size_t>(n);
   std::vector<T> out(dims * count);
-  in.read(reinterpret_cast<char*>(out.data()), static_cast<std::streamsize>(sizeof(T) * out.size()));
+  const auto want = static_cast<std::streamsize>(sizeof(T) * out.size());
+  in.read(reinterpret_cast<char*>(out.data()), want);
+  if (in.gcount() != want) {
+    std::cerr << "File " << path << " is truncated: " << count << " x " << dims << " values expected"
+              << std::endl;
+    std::exit(1);
+  }
   return out;
 }
 
