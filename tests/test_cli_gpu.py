@@ -64,3 +64,18 @@ def test_cli_refuses_short_query_files(cli, u8_index, tmp_path):
     header_only.write_bytes(b"\x01\x00")
     r = _run(cli, "--index-dir", d, "--query", header_only, "--data-type", "uint8", "--repeat", 1)
     assert r.returncode == 1 and "Invalid header" in r.stderr
+
+
+@pytest.mark.parametrize("policy", ["none", "gpruning"])
+def test_reference_python_api_through_this_cli(cli, u8_index, policy):
+    """The whole drop-in chain: IndexQuiver (the reference's Python API, unchanged) runs this CLI, which runs
+    the engine; the arrays it returns are the engine's own results for the same queries and options."""
+    from quiver import IndexQuiver
+    from quiver_b200 import Engine, SearchParams
+    idx = IndexQuiver(u8_index["dir"], data_type="uint8", binary=cli)
+    ids, dists = idx.search(u8_index["queries"].astype(np.uint8), topk=10, ef_search=45, early_exit_policy=policy)
+    p = SearchParams(topk=10, ef_search=45, pipe_width=2, early_exit_policy=policy)
+    with Engine.open(u8_index["dir"], "uint8") as eng:
+        ref_ids, ref_dists, _ = eng.search(u8_index["queries"], p)
+    np.testing.assert_array_equal(ids, ref_ids)
+    np.testing.assert_array_equal(dists.view(np.uint32), ref_dists.view(np.uint32))
