@@ -68,8 +68,9 @@ def test_cli_refuses_short_query_files(cli, u8_index, tmp_path):
 
 @pytest.mark.parametrize("policy", ["none", "gpruning"])
 def test_reference_python_api_through_this_cli(cli, u8_index, policy):
-    """The whole drop-in chain: IndexQuiver (the reference's Python API, unchanged) runs this CLI, which runs
-    the engine; the arrays it returns are the engine's own results for the same queries and options."""
+    """The whole drop-in chain: IndexQuiver (the reference's Python API, as this repository's front end
+    implements it) runs this CLI, which runs the engine; the arrays it returns are the engine's own results
+    for the same queries and options."""
     from quiver import IndexQuiver
     from quiver_b200 import Engine, SearchParams
     idx = IndexQuiver(u8_index["dir"], data_type="uint8", binary=cli)
