@@ -253,14 +253,18 @@ int qv_check_device_status(qv_engine* engine);
  * pressure).  This entry point has no counterpart in the reference.  The
  * search kernel's scratch -- work counter, error words and device copies of
  * the queries and results -- is a file-scope device array of
- * QV_NOALLOC_SCRATCH_BYTES held by every GPU that loads the library, so a
- * call may carry at most
+ * QV_NOALLOC_SCRATCH_BYTES, so a call may carry at most
  *   256 + align256(nq*dim*4) + 2*align256(nq*topk*4) + align256(nq*4)
  * bytes (about 7,000 queries of 128 dims at top-10); larger batches are
- * rejected with QV_ERR_INVALID_ARG.  The first call on a device looks up the
- * array's address with that device current; make it before any stream
- * capture.  Calls share the array: calls that overlap on the GPU race and
- * must be serialised by the caller.  Results equal qv_search's. */
+ * rejected with QV_ERR_INVALID_ARG before anything is copied or launched.
+ * qv_engine_create / qv_engine_create_from_arrays, with the engine's device
+ * current, look up the array's device address and load the search kernels,
+ * so the array is placed on the device when the index is loaded (under
+ * CUDA's lazy module loading too) and stays until the process exits; the
+ * address does not survive a reset of the device's context.  Calls share
+ * the array and it keeps the last call's contents: calls that overlap on
+ * the GPU race and must be serialised by the caller.  Results equal
+ * qv_search's. */
 #define QV_NOALLOC_SCRATCH_BYTES (4u << 20)
 int qv_search_noalloc(qv_engine* engine, const float* queries, int64_t nq, int64_t dim,
                       const qv_search_opts* opts, int32_t* ids, float* dists,

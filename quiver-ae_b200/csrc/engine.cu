@@ -14,7 +14,6 @@
 #include <cstdio>
 #include <cstring>
 #include <memory>
-#include <mutex>
 #include <numeric>
 #include <string>
 #include <vector>
@@ -84,6 +83,8 @@ struct qv_engine {
   float* d_centroid = nullptr;
   int32_t* d_chunk_off = nullptr;
   int32_t* d_scratch = nullptr;  // [0] work counter, [1..4] error info
+  // device address of g_qv_noalloc_scratch on `device`, resolved at creation
+  unsigned char* d_noalloc = nullptr;
   int num_sms = 0;
   int max_smem_optin = 0;
   cudaStream_t stream = nullptr;
@@ -170,12 +171,26 @@ void validate_opts(const qv_engine* e, const qv_search_opts& o) {
   (void)e;
 }
 
+// Kernel specialisation for this index: neighbours per lane and PQ width.
+void set_kernel_shape(const qv_engine* e, Plan& pl) {
+  pl.smax = e->L.max_degree <= 64 ? 2 : 4;
+  pl.mc = e->M == 32 ? 32 : 0;
+}
+
+// Binds pl.fn / pl.fn_stream for the index's element type, pl.block, pl.mc and pl.smax.
+void bind_kernels(const qv_engine* e, Plan& pl) {
+  switch (e->L.data_type) {
+    case QV_UINT8: qv::bind_search_u8(pl); break;
+    case QV_INT8: qv::bind_search_i8(pl); break;
+    default: qv::bind_search_f32(pl); break;
+  }
+}
+
 Plan make_plan(qv_engine* e, const qv_search_opts& o, int64_t nq) {
   validate_opts(e, o);
   Plan pl;
   const auto& L = e->L;
-  pl.smax = L.max_degree <= 64 ? 2 : 4;
-  pl.mc = e->M == 32 ? 32 : 0;
+  set_kernel_shape(e, pl);
   // --queries-per-block 0/1: one query per 128-thread CTA (the block kernel);
   // Q >= 2: Q one-warp query slots per CTA (the warp kernel).  Both give
   // identical results.
@@ -220,11 +235,7 @@ Plan make_plan(qv_engine* e, const qv_search_opts& o, int64_t nq) {
     fail(QV_ERR_UNSUPPORTED, "one query slot needs " + std::to_string(y.bytes) +
                                  " B of shared memory, above the per-CTA limit");
 
-  switch (L.data_type) {
-    case QV_UINT8: qv::bind_search_u8(pl); break;
-    case QV_INT8: qv::bind_search_i8(pl); break;
-    default: qv::bind_search_f32(pl); break;
-  }
+  bind_kernels(e, pl);
   CK(cudaFuncSetAttribute(pl.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, e->max_smem_optin));
   CK(cudaFuncSetAttribute(pl.fn_stream, cudaFuncAttributeMaxDynamicSharedMemorySize, e->max_smem_optin));
 
@@ -342,9 +353,9 @@ void enqueue_search(qv_engine* e, const Plan& pl, const qvk::SearchParams& p, cu
   CK(cudaGetLastError());
 }
 
-void read_device_status(qv_engine* e) {
-  int32_t info[4];
-  CK(cudaMemcpy(info, e->d_scratch + 1, sizeof(info), cudaMemcpyDeviceToHost));
+// Throws QV_ERR_DEVICE describing the search kernel's error words
+// {code, query, node or step, spare} unless code is kErrNone.
+void raise_device_error(const int32_t info[4]) {
   if (info[0] == qvk::kErrNone) return;
   const char* what = info[0] == qvk::kErrNeighborRange ? "a neighbour id >= num_points"
                    : info[0] == qvk::kErrDegree        ? "a stored degree above R"
@@ -355,6 +366,62 @@ void read_device_status(qv_engine* e) {
                                                        : "an unknown device error";
   fail(QV_ERR_DEVICE, std::string("search kernel found ") + what + " (query " +
                           std::to_string(info[1]) + ", node/step " + std::to_string(info[2]) + ")");
+}
+
+void read_device_status(qv_engine* e) {
+  int32_t info[4];
+  CK(cudaMemcpy(info, e->d_scratch + 1, sizeof(info), cudaMemcpyDeviceToHost));
+  raise_device_error(info);
+}
+
+}  // namespace
+
+// ------------------------------------------------- no-alloc scratch array --
+//
+// qv_search_noalloc serves callers that may not allocate device memory on
+// their search path: plugins whose host application owns the device
+// allocator and forbids them from calling cudaMalloc, and serving loops
+// where a cudaMalloc (with its implicit device synchronisation) or a failed
+// allocation under memory pressure is not acceptable once the index is
+// loaded.  The search kernel's scratch -- its work counter, its error words
+// and the device copies of the queries and results -- lives in the
+// file-scope array below instead of engine-owned allocations.  The array
+// is 4 MiB.  Engine creation (qv_engine_create / _from_arrays), with the
+// engine's device current, looks up the array's device address and loads
+// the search kernels a no-alloc call can launch, so that under CUDA's lazy
+// module loading the array and the kernels' code are placed on the device
+// while the index is loaded, not by the first no-alloc call; from then on
+// the device holds the array until the process exits.  The address is kept
+// in the engine: an engine does not survive a reset of its device's
+// context (cudaDeviceReset), and neither does the address.  All calls share
+// the array and it keeps the last call's contents; the work counter and
+// error words are cleared at the start of every call.  Calls that overlap
+// on the GPU (two host threads, or two engines on one device) race on the
+// array and must be serialised by the caller.
+static __device__ __align__(256) unsigned char g_qv_noalloc_scratch[QV_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+
+constexpr size_t kNoallocHeader = 256;  // work counter + 4 error words, padded
+
+size_t align256(size_t v) { return (v + 255) / 256 * 256; }
+
+// With e->device current: resolve g_qv_noalloc_scratch's device address and
+// load every search kernel qv_search_noalloc may launch for this index.
+void prepare_noalloc(qv_engine* e) {
+  void* ptr = nullptr;
+  const cudaError_t rc = cudaGetSymbolAddress(&ptr, g_qv_noalloc_scratch);
+  if (rc != cudaSuccess)
+    fail(QV_ERR_CUDA, std::string("cudaGetSymbolAddress(g_qv_noalloc_scratch) failed: ") + cudaGetErrorString(rc));
+  e->d_noalloc = static_cast<unsigned char*>(ptr);
+  Plan pl;
+  set_kernel_shape(e, pl);
+  for (const bool block : {true, false}) {
+    pl.block = block;
+    bind_kernels(e, pl);
+    cudaFuncAttributes attr;
+    CK(cudaFuncGetAttributes(&attr, pl.fn));
+  }
 }
 
 // ------------------------------------------------------ engine set-up --
@@ -371,6 +438,7 @@ void init_device_side(qv_engine* e, int device) {
   for (auto& ev : e->ev) CK(cudaEventCreate(&ev));
   CK(cudaMalloc(&e->d_scratch, 8 * sizeof(int32_t)));
   CK(cudaMemset(e->d_scratch, 0, 8 * sizeof(int32_t)));
+  prepare_noalloc(e);
 }
 
 void upload_pq(qv_engine* e, const float* pivots, const float* centroid, const int32_t* chunk_off,
@@ -1116,50 +1184,7 @@ int qv_check_device_status(qv_engine* e) {
 
 
 // ---------------------------------------------------- scratch-free search --
-//
-// qv_search_noalloc serves callers that may not allocate device memory on
-// their search path: plugins whose host application owns the device
-// allocator and forbids them from calling cudaMalloc, and serving loops
-// where a cudaMalloc (with its implicit device synchronisation) or a failed
-// allocation under memory pressure is not acceptable once the index is
-// loaded.  The search kernel's scratch -- its work counter, its error words
-// and the device copies of the queries and results -- lives in the
-// file-scope array below instead of engine-owned allocations.  The array
-// is 4 MiB; every GPU that loads this library holds it until the process
-// exits.  Its device address is looked up once per device, by the first
-// call on that device with that device current; make that first call
-// before any stream capture.  All calls share the array and it keeps the
-// last call's contents; the work counter and error words are cleared at the
-// start of every call.  Calls that overlap on the GPU (two host threads, or
-// two engines on one device) race on the array and must be serialised by
-// the caller.
-static __device__ __align__(256) unsigned char g_qv_noalloc_scratch[QV_NOALLOC_SCRATCH_BYTES];
-
-namespace {
-
-constexpr int kNoallocMaxDevices = 64;
-constexpr size_t kNoallocHeader = 256;  // work counter + 4 error words, padded
-std::mutex g_noalloc_mu;
-unsigned char* g_noalloc_base[kNoallocMaxDevices] = {};
-
-// Device address of g_qv_noalloc_scratch on `device` (which must be current).
-unsigned char* noalloc_base(int device) {
-  if (device < 0 || device >= kNoallocMaxDevices)
-    fail(QV_ERR_UNSUPPORTED, "qv_search_noalloc supports CUDA ordinals below 64");
-  std::lock_guard<std::mutex> lock(g_noalloc_mu);
-  if (!g_noalloc_base[device]) {
-    void* ptr = nullptr;
-    const cudaError_t rc = cudaGetSymbolAddress(&ptr, g_qv_noalloc_scratch);
-    if (rc != cudaSuccess)
-      fail(QV_ERR_CUDA, std::string("cudaGetSymbolAddress(g_qv_noalloc_scratch) failed: ") + cudaGetErrorString(rc));
-    g_noalloc_base[device] = static_cast<unsigned char*>(ptr);
-  }
-  return g_noalloc_base[device];
-}
-
-size_t align256(size_t v) { return (v + 255) / 256 * 256; }
-
-}  // namespace
+// (the scratch array and its set-up are defined before engine set-up)
 
 int qv_search_noalloc(qv_engine* e, const float* queries, int64_t nq, int64_t dim, const qv_search_opts* opts,
                       int32_t* ids, float* dists, int32_t* found) {
@@ -1171,10 +1196,19 @@ int qv_search_noalloc(qv_engine* e, const float* queries, int64_t nq, int64_t di
                                    " dims, but the index expects " + std::to_string(e->L.dim));
     if (opts->visited_filter)
       fail(QV_ERR_UNSUPPORTED, "the visited-filter mode needs per-CTA device tables; use qv_search");
+    if (!e->d_noalloc) fail(QV_ERR_INVALID_ARG, "engine has no scratch address");
     CK(cudaSetDevice(e->device));
     const Plan pl = make_plan(e, *opts, std::max<int64_t>(nq, 1));
     if (nq == 0) return;
     const size_t k = static_cast<size_t>(opts->topk);
+    // Bound nq before any product of it: every query needs dim*4 + 2*k*4 + 4
+    // bytes of the array (before alignment), so a larger nq can never fit.
+    const size_t per_query = static_cast<size_t>(dim) * 4 + 2 * k * 4 + 4;
+    if (static_cast<uint64_t>(nq) > (QV_NOALLOC_SCRATCH_BYTES - kNoallocHeader) / per_query)
+      fail(QV_ERR_INVALID_ARG, "qv_search_noalloc: " + std::to_string(nq) + " queries of " +
+                                   std::to_string(per_query) + " bytes of scratch each are above its " +
+                                   std::to_string(QV_NOALLOC_SCRATCH_BYTES) +
+                                   "-byte maximum; split the batch or use qv_search");
     const size_t q_bytes = align256(static_cast<size_t>(nq) * dim * 4);
     const size_t r_bytes = align256(static_cast<size_t>(nq) * k * 4);
     const size_t f_bytes = align256(static_cast<size_t>(nq) * 4);
@@ -1183,7 +1217,7 @@ int qv_search_noalloc(qv_engine* e, const float* queries, int64_t nq, int64_t di
       fail(QV_ERR_INVALID_ARG, "qv_search_noalloc: " + std::to_string(nq) + " queries need " + std::to_string(need) +
                                    " bytes of scratch, above its " + std::to_string(QV_NOALLOC_SCRATCH_BYTES) +
                                    "-byte maximum; split the batch or use qv_search");
-    unsigned char* base = noalloc_base(e->device);
+    unsigned char* base = e->d_noalloc;
     int32_t* counters = reinterpret_cast<int32_t*>(base);
     float* d_q = reinterpret_cast<float*>(base + kNoallocHeader);
     int32_t* d_ids = reinterpret_cast<int32_t*>(base + kNoallocHeader + q_bytes);
@@ -1203,9 +1237,7 @@ int qv_search_noalloc(qv_engine* e, const float* queries, int64_t nq, int64_t di
     int32_t info[4];
     CK(cudaMemcpyAsync(info, counters + 1, sizeof(info), cudaMemcpyDeviceToHost, st));
     CK(cudaStreamSynchronize(st));
-    if (info[0] != qvk::kErrNone)
-      fail(QV_ERR_DEVICE, "search kernel reported device error " + std::to_string(info[0]) + " (query " +
-                              std::to_string(info[1]) + ")");
+    raise_device_error(info);
   });
 }
 int qv_build_lut_device(qv_engine* e, const float* d_queries, int64_t nq, float* d_lut, float* d_q2,
