@@ -19,21 +19,34 @@ import numpy as np
 
 HERE = Path(__file__).resolve().parent
 LIB = HERE / "_ref" / "libref_quiver.so"
-REFERENCE_SRC = Path(os.environ.get("QUIVER_REFERENCE_SRC", "/root/reference/src"))
+
+
+def reference_root() -> Path | None:
+    """The reference project's checkout: $QUIVER_REFERENCE, else the ``reference_path`` that the repository's
+    BASELINE.json records; None when neither names an existing directory."""
+    where = os.environ.get("QUIVER_REFERENCE")
+    if not where:
+        baseline = HERE.parent / "BASELINE.json"
+        if baseline.is_file():
+            import json
+            where = json.loads(baseline.read_text()).get("reference_path")
+    return Path(where) if where and Path(where).is_dir() else None
 
 
 def build_if_available(force: bool = False) -> Path | None:
-    """Compile the harness when the reference sources are on this machine."""
-    kernel = REFERENCE_SRC / "quiver" / "kernel_core" / "kernel_q1.cuh"
-    if not kernel.exists():
+    """Compile the harness when the reference sources are on this machine (see reference_root)."""
+    root = reference_root()
+    kernel = root / "src" / "quiver" / "kernel_core" / "kernel_q1.cuh" if root else None
+    if kernel is None or not kernel.exists():
         return LIB if LIB.exists() else None
+    reference_src = root / "src"
     src = HERE / "ref_harness.cu"
     if not force and LIB.exists() and LIB.stat().st_mtime >= src.stat().st_mtime:
         return LIB
     nvcc = shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
     LIB.parent.mkdir(exist_ok=True)
     cmd = [nvcc, "-gencode", "arch=compute_100a,code=sm_100a", "-O2", "-std=c++17", "-Xcompiler", "-fPIC",
-           "-shared", "-I", str(REFERENCE_SRC), str(src), "-o", str(LIB)]
+           "-shared", "-I", str(reference_src), str(src), "-o", str(LIB)]
     res = subprocess.run(cmd, capture_output=True, text=True)
     if res.returncode != 0:
         raise RuntimeError(f"reference harness build failed:\n{res.stderr}")

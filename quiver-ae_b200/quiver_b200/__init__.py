@@ -6,6 +6,7 @@ persistent sm_100a kernel behind the C ABI in ``include/quiver_b200.h``.
 """
 from ._lib import NativeLibraryMissing
 from .engine import Engine, QuiverEngineError, SearchParams
+from .index import IndexQuiver, QuiverError
 
-__all__ = ["Engine", "SearchParams", "QuiverEngineError", "NativeLibraryMissing"]
+__all__ = ["Engine", "SearchParams", "QuiverEngineError", "NativeLibraryMissing", "IndexQuiver", "QuiverError"]
 __version__ = "0.1.0"

@@ -57,3 +57,24 @@ def odd_index(tmp_path_factory):
     """Uncommon shapes: R=100 (>64 neighbours per node), M=12 (generic code path), dim=48."""
     return _make_index(tmp_path_factory.mktemp("idx"), "odd", n=2500, dim=48, dtype="uint8", centers=6,
                        sigma=25.0, R=100, L=110, M=12, nq=48, seed=13)
+
+
+def reference_python_root() -> Path:
+    """Where the reference's unmodified Python package (``quiver``) is installed: $QUIVER_REFERENCE_PY, else
+    baseline/_ref (``__graft_entry__.build()`` installs it there from the reference sources when they are
+    present)."""
+    import os
+    return Path(os.environ.get("QUIVER_REFERENCE_PY", REPO / "baseline" / "_ref"))
+
+
+@pytest.fixture(scope="session")
+def reference_quiver():
+    """The reference's own ``quiver`` module, imported unchanged; skips when it is not installed."""
+    root = reference_python_root()
+    if not (root / "quiver" / "index.py").is_file():
+        pytest.skip(f"the reference's Python package is not installed under {root}")
+    if str(root) not in sys.path:
+        sys.path.insert(0, str(root))
+    import quiver
+    assert Path(quiver.__file__).resolve().is_relative_to(root.resolve()), quiver.__file__
+    return quiver

@@ -1,41 +1,22 @@
-"""IndexQuiver: the reference's Python API contract (python/tests/test_index.py
-in ruc-system/quiver-ae) held by this repository's front end, plus the CLI's
-argument validation, which runs before any device work."""
+"""The Python search API.
+
+* ``quiver_b200.IndexQuiver``, the in-process front end: the reference's
+  constructor and ``search`` arguments (python/quiver/index.py:27-116), with
+  the same ``ValueError`` messages as the reference's module for every bad
+  argument, checked side by side against that module, unchanged, when it is
+  installed (baseline/_ref or $QUIVER_REFERENCE_PY).
+* The reference's module itself finds this repository's CLI through
+  ``QUIVER_BINARY`` (index.py:244-264).
+* The CLI's argument validation, which runs before any device work.
+"""
 from __future__ import annotations
 
-import stat
 import struct
 import subprocess
 from pathlib import Path
 
 import numpy as np
 import pytest
-
-ENGINE_STUB = r'''#!/usr/bin/env python3
-import struct, sys
-from pathlib import Path
-import numpy as np
-
-argv = sys.argv[1:]
-get = lambda flag: argv[argv.index(flag) + 1]
-with open(get("--query"), "rb") as f:
-    n, d = struct.unpack("<ii", f.read(8))
-k = int(get("--topk"))
-if "--ssd-list-file" in argv:
-    lines = [l for l in Path(get("--ssd-list-file")).read_text().splitlines() if l]
-    assert lines == ["0000:01:00.0", "0000:02:00.0"], lines
-Path(get("--result-prefix") + ".argv").write_text("\n".join(argv))
-for suffix, arr in (("_ids.bin", np.arange(n * k, dtype="<i4")),
-                    ("_distances.bin", np.arange(n * k, dtype="<f4") / 10)):
-    with open(get("--result-prefix") + suffix, "wb") as f:
-        f.write(struct.pack("<ii", n, k) + arr.tobytes())
-'''
-
-
-def _exe(path: Path, text: str) -> Path:
-    path.write_text(text)
-    path.chmod(path.stat().st_mode | stat.S_IXUSR)
-    return path
 
 
 @pytest.fixture()
@@ -45,81 +26,90 @@ def index_dir(tmp_path):
     return d
 
 
-def test_results_and_ssd_list(tmp_path, index_dir):
-    from quiver import IndexQuiver
-    eng = _exe(tmp_path / "quiver_search", ENGINE_STUB)
-    idx = IndexQuiver(index_dir, data_type="float32", ssds=["0000:01:00.0", "0000:02:00.0"], binary=eng)
-    ids, dists = idx.search(np.ones((3, 4), dtype=np.float64), topk=2)
-    assert idx.num_ssds == 2
-    assert ids.dtype == np.dtype("<i4") and dists.dtype == np.dtype("<f4")
-    np.testing.assert_array_equal(ids, [[0, 1], [2, 3], [4, 5]])
-    np.testing.assert_allclose(dists, [[0.0, 0.1], [0.2, 0.3], [0.4, 0.5]])
+# (constructor kwargs, search kwargs or None) -> each raises ValueError in both front ends
+BAD_ARGUMENTS = [
+    ({"data_type": "float16"}, None),
+    ({"pipe_width": 0}, None),
+    ({"num_blocks": -3}, None),
+    ({"queries_per_block": 0}, None),
+    ({"poll_threads": 0}, None),
+    ({"runners_per_ssd": 0}, None),
+    ({"memory_backend": "disk"}, None),
+    ({"ssds": ["0000:01:00.0", " "]}, None),
+    ({"spdk_base_lba": -1}, None),
+    ({"ssd_list_file": "/nonexistent/ssds.txt"}, None),
+    ({}, {"topk": 0}),
+    ({}, {"ef_search": -1}),
+    ({}, {"early_exit_policy": "darth"}),
+    ({}, {"timeout": 0}),
+    ({}, {"queries": np.ones((0, 4))}),
+    ({}, {"queries": np.ones((2, 2, 2))}),
+]
 
 
-def test_argv_contract(tmp_path, index_dir, monkeypatch):
-    """The flags a caller sees on the engine's command line (index.py:136-169)."""
-    from quiver import IndexQuiver
-    eng = _exe(tmp_path / "quiver_search", ENGINE_STUB)
-    seen = {}
-    real_run = subprocess.run
-
-    def spy(cmd, **kw):
-        seen["argv"] = cmd
-        return real_run(cmd, **kw)
-
-    monkeypatch.setattr(subprocess, "run", spy)
-    IndexQuiver(index_dir, data_type="uint8", binary=eng, pipe_width=4, queries_per_block=2).search(
-        np.ones((2, 8)), topk=5, ef_search=70, early_exit_policy="none")
-    argv = seen["argv"]
-    flag = lambda f: argv[argv.index(f) + 1]
-    assert flag("--data-type") == "uint8" and flag("--topk") == "5" and flag("--ef-search") == "70"
-    assert flag("--repeat") == "1" and flag("--pipe-width") == "4" and flag("--queries-per-block") == "2"
-    assert flag("--num-blocks") == "756" and flag("--early-exit-policy") == "none"
-    assert flag("--query").endswith(".u8bin") and "--ssd-list-file" not in argv
+def _error_of(cls, index_dir, ctor, search, binary):
+    try:
+        extra = {"binary": binary} if binary is not None else {}
+        idx = cls(index_dir, **ctor, **extra)
+        if search is not None:
+            kw = dict(search)
+            q = kw.pop("queries", np.ones((1, 4), np.float32))
+            idx.search(q, **kw)
+    except ValueError as err:
+        return str(err)
+    return None
 
 
-def test_rejects_conflicting_ssd_configuration(tmp_path, index_dir):
-    from quiver import IndexQuiver
-    eng = _exe(tmp_path / "quiver_search", ENGINE_STUB)
+@pytest.mark.parametrize("ctor,search", BAD_ARGUMENTS)
+def test_front_end_refuses_bad_arguments(index_dir, ctor, search):
+    from quiver_b200 import IndexQuiver
+    assert _error_of(IndexQuiver, index_dir, ctor, search, None) is not None
+
+
+@pytest.mark.parametrize("ctor,search", BAD_ARGUMENTS)
+def test_front_end_messages_match_the_reference_module(reference_quiver, index_dir, tmp_path, ctor, search):
+    """Same ValueError text as the reference's unmodified module for the same bad argument (the reference
+    needs an executable to construct; a stub that is never run stands in)."""
+    from quiver_b200 import IndexQuiver
+    stub = tmp_path / "quiver_search"
+    stub.write_text("#!/bin/sh\nexit 3\n")
+    stub.chmod(0o755)
+    want = _error_of(reference_quiver.IndexQuiver, index_dir, ctor, search, stub)
+    got = _error_of(IndexQuiver, index_dir, ctor, search, None)
+    assert want is not None
+    assert got == want
+
+
+def test_front_end_directory_and_ssd_conflict(index_dir, tmp_path):
+    from quiver_b200 import IndexQuiver
+    with pytest.raises(ValueError, match="index_dir is not a directory"):
+        IndexQuiver(tmp_path / "missing")
     lst = tmp_path / "ssds.txt"
-    lst.write_text("0000:01:00.0\n")
+    lst.write_text("0000:01:00.0\n# comment\n\n0000:02:00.0\n")
     with pytest.raises(ValueError, match="either ssds or ssd_list_file"):
-        IndexQuiver(index_dir, ssds=["0000:01:00.0"], ssd_list_file=lst, binary=eng)
+        IndexQuiver(index_dir, ssds=["0000:01:00.0"], ssd_list_file=lst)
+    assert IndexQuiver(index_dir, ssd_list_file=lst).num_ssds == 2
+    assert IndexQuiver(index_dir, ssds=["a", "b", "c"]).num_ssds == 3
 
 
-def test_validation_errors(tmp_path, index_dir):
-    from quiver import IndexQuiver
-    eng = _exe(tmp_path / "quiver_search", ENGINE_STUB)
-    with pytest.raises(ValueError, match="data_type"):
-        IndexQuiver(index_dir, data_type="float16", binary=eng)
-    with pytest.raises(ValueError, match="pipe_width must be positive"):
-        IndexQuiver(index_dir, pipe_width=0, binary=eng)
-    idx = IndexQuiver(index_dir, binary=eng)
-    with pytest.raises(ValueError, match="early_exit_policy"):
-        idx.search(np.ones((1, 4)), early_exit_policy="darth")
-    with pytest.raises(ValueError, match="non-empty"):
-        idx.search(np.ones((0, 4)))
+def test_front_end_refuses_ssds_and_unknown_flags_before_loading(index_dir):
+    """No SPDK here: a search with SSDs configured fails as in a build without SPDK, before the index is
+    opened; CLI flags the in-process engine does not take are refused the same way."""
+    from quiver_b200 import IndexQuiver, QuiverError
+    with pytest.raises(QuiverError, match="without SPDK support"):
+        IndexQuiver(index_dir, ssds=["0000:01:00.0"]).search(np.ones((1, 4), np.float32))
+    idx = IndexQuiver(index_dir)
+    with pytest.raises(QuiverError, match="not supported by the in-process engine"):
+        idx.search(np.ones((1, 4), np.float32), extra_args=["--per-step-recall"])
+    assert idx._engine is None
 
 
-def test_reports_engine_failure(tmp_path, index_dir):
-    from quiver import IndexQuiver, QuiverError
-    eng = _exe(tmp_path / "quiver_search", "#!/usr/bin/env sh\necho 'index metadata is invalid' >&2\nexit 7\n")
-    with pytest.raises(QuiverError, match="code 7: index metadata is invalid"):
-        IndexQuiver(index_dir, binary=eng).search(np.ones((1, 4), dtype=np.float32))
-
-
-def test_reports_engine_timeout(tmp_path, index_dir):
-    from quiver import IndexQuiver, QuiverError
-    eng = _exe(tmp_path / "quiver_search", "#!/usr/bin/env python3\nwhile True:\n    pass\n")
-    with pytest.raises(QuiverError, match="exceeded the 0.05 second timeout"):
-        IndexQuiver(index_dir, binary=eng).search(np.ones((1, 4), dtype=np.float32), timeout=0.05)
-
-
-def test_missing_result_file(tmp_path, index_dir):
-    from quiver import IndexQuiver, QuiverError
-    eng = _exe(tmp_path / "quiver_search", "#!/usr/bin/env sh\nexit 0\n")
-    with pytest.raises(QuiverError, match="did not create result_ids.bin"):
-        IndexQuiver(index_dir, binary=eng).search(np.ones((1, 4), dtype=np.float32))
+def test_reference_module_finds_this_cli(reference_quiver, index_dir, monkeypatch):
+    """The reference's module, unchanged, resolves QUIVER_BINARY to this repository's CLI."""
+    from quiver_b200 import _build
+    cli = _build.build_cli()
+    monkeypatch.setenv("QUIVER_BINARY", str(cli))
+    assert reference_quiver.IndexQuiver(index_dir).binary == Path(cli).resolve()
 
 
 # ------------------------------------------------ the real quiver_search --
@@ -133,13 +123,6 @@ def cli():
 
 def _run(cli, *args):
     return subprocess.run([str(cli), *map(str, args)], capture_output=True, text=True, timeout=60)
-
-
-def test_default_binary_is_this_build(index_dir, cli, monkeypatch):
-    from quiver import IndexQuiver
-    monkeypatch.delenv("QUIVER_BINARY", raising=False)
-    monkeypatch.setenv("PATH", "/usr/bin:/bin")
-    assert IndexQuiver(index_dir).binary == Path(cli).resolve()
 
 
 @pytest.mark.parametrize("args,msg", [

@@ -1,6 +1,7 @@
 """The drop-in CLI on a B200: bin/quiver_search, run on an index directory the way the reference's Python
 API runs its binary, writes the engine's ids and distances bit for bit, prints the reference's report lines
-with the recall of what it wrote, and refuses query files whose header or data is short."""
+with the recall of what it wrote, and refuses query files whose header or data is short.  The reference's
+own Python package drives it unchanged, and the in-process front end returns what that chain returns."""
 from __future__ import annotations
 
 import re
@@ -67,16 +68,35 @@ def test_cli_refuses_short_query_files(cli, u8_index, tmp_path):
 
 
 @pytest.mark.parametrize("policy", ["none", "gpruning"])
-def test_reference_python_api_through_this_cli(cli, u8_index, policy):
-    """The whole drop-in chain: IndexQuiver (the reference's Python API, as this repository's front end
-    implements it) runs this CLI, which runs the engine; the arrays it returns are the engine's own results
-    for the same queries and options."""
-    from quiver import IndexQuiver
+def test_reference_python_api_through_this_cli(cli, u8_index, reference_quiver, monkeypatch, policy):
+    """The whole drop-in chain: the reference's own Python package, unmodified (installed under
+    baseline/_ref from the reference sources), finds this CLI through QUIVER_BINARY and runs it; the arrays
+    it returns are the engine's own results for the same queries and options."""
     from quiver_b200 import Engine, SearchParams
-    idx = IndexQuiver(u8_index["dir"], data_type="uint8", binary=cli)
+    monkeypatch.setenv("QUIVER_BINARY", str(cli))
+    idx = reference_quiver.IndexQuiver(u8_index["dir"], data_type="uint8")
     ids, dists = idx.search(u8_index["queries"].astype(np.uint8), topk=10, ef_search=45, early_exit_policy=policy)
     p = SearchParams(topk=10, ef_search=45, pipe_width=2, early_exit_policy=policy)
     with Engine.open(u8_index["dir"], "uint8") as eng:
         ref_ids, ref_dists, _ = eng.search(u8_index["queries"], p)
     np.testing.assert_array_equal(ids, ref_ids)
     np.testing.assert_array_equal(dists.view(np.uint32), ref_dists.view(np.uint32))
+
+
+@pytest.mark.parametrize("policy", ["none", "gpruning"])
+def test_in_process_front_end_matches_the_reference_module(cli, u8_index, reference_quiver, monkeypatch, policy):
+    """quiver_b200.IndexQuiver (in process, index kept resident) returns what the reference's module returns
+    through this CLI, for the same arguments, on two calls in a row; the same holds for float32 queries that
+    the front end first narrows to the index's uint8 as the reference does."""
+    from quiver_b200 import IndexQuiver
+    monkeypatch.setenv("QUIVER_BINARY", str(cli))
+    ref = reference_quiver.IndexQuiver(u8_index["dir"], data_type="uint8", pipe_width=4, queries_per_block=2)
+    q = u8_index["queries"] + 0.25
+    want = ref.search(q, topk=12, ef_search=60, early_exit_policy=policy)
+    with IndexQuiver(u8_index["dir"], data_type="uint8", pipe_width=4, queries_per_block=2) as idx:
+        for _ in range(2):
+            got = idx.search(q, topk=12, ef_search=60, early_exit_policy=policy)
+            np.testing.assert_array_equal(got[0], want[0])
+            np.testing.assert_array_equal(got[1].view(np.uint32), want[1].view(np.uint32))
+        one = idx.search(q[3], topk=12, ef_search=60, early_exit_policy=policy)
+        np.testing.assert_array_equal(one[0][0], want[0][3])
