@@ -11,6 +11,12 @@ smallest ef_search from a fixed ladder whose Recall@10 reaches the target
 N > 1 runs under torchrun: each rank holds a replica of the index and
 searches its own 10K-query batch per step (weak scaling, no collective on
 the data path; the barrier and the max-over-ranks timing use NCCL).
+
+Besides the headline (HBM page store), the line carries: ``latency_mode``
+(batches of 1, 4 and 16 end to end), ``host_pages`` at N = 1 (node records
+read over PCIe from pinned host DRAM, config 2's layout) and ``striped`` at
+N > 1 (the page store striped over the ranks' GPUs and read over NVLink,
+the 1B layout), each at the same ef and queries as the headline.
 """
 from __future__ import annotations
 
@@ -32,7 +38,9 @@ sys.path.insert(0, str(ROOT / "quiver-ae_b200"))
 sys.path.insert(0, str(ROOT))
 
 METRIC = "QPS at Recall@10=0.90 and P99 latency (ms), 1/2/4/8 B200, 1B×128 uint8"
-EF_LADDER = (45, 60, 80, 100, 120, 150, 180, 220, 260, 320, 400)
+# ef_search values tried in order; the engine accepts up to 4096 (lists above 512 entries merge record by record)
+EF_LADDER = (45, 60, 80, 100, 120, 150, 180, 220, 260, 320, 400, 512, 640, 800, 1024, 1280, 1600, 2048, 2560,
+             3200, 4096)
 CALIB_QUERIES = 2000
 
 
@@ -66,6 +74,56 @@ def read_peaks() -> dict:
         d = json.loads(p.read_text())
         return {"hbm_gbs": float(d["hbm_gbs"]), "source": "measured"}
     return {"hbm_gbs": 6650.0, "source": "fallback"}
+
+
+def read_nvlink_peak() -> dict:
+    """Per-direction NVLink peer bandwidth per GPU: MEASURED_PEAKS.json's figure when it has one, else the
+    pool's measured peer copy (770 GB/s per direction; 900 nominal)."""
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        for key in ("nvlink_gbs", "p2p_gbs"):
+            if key in d:
+                return {"gbs": float(d[key]), "source": "measured"}
+    return {"gbs": 770.0, "source": "pool peer-copy measurement (fallback)"}
+
+
+def time_steps(eng, dq, p, d_ids, d_dists, stream, steps: int, warmup: int, barrier, device):
+    """`warmup` untimed launches, then `steps` timed ones with CUDA events on `stream`, bracketed by barriers;
+    returns (per-step ms on this rank, max over ranks of the total ms)."""
+    import torch
+    from quiver_b200 import shard
+    for _ in range(warmup):
+        eng.search_device(dq, p, d_ids, d_dists, stream=stream.cuda_stream)
+    barrier()
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
+    evs[0].record(stream)
+    for i in range(steps):
+        eng.search_device(dq, p, d_ids, d_dists, stream=stream.cuda_stream)
+        evs[i + 1].record(stream)
+    torch.cuda.synchronize()
+    eng.check_device_status()
+    step_ms = [evs[i].elapsed_time(evs[i + 1]) for i in range(steps)]
+    total_ms = shard.reduce_max(evs[0].elapsed_time(evs[-1]), device=device)
+    barrier()
+    return step_ms, total_ms
+
+
+def pcie_h2d_gbs(dev) -> float:
+    """Host-to-device copy rate of a pinned 1 GiB buffer on this box (best of 3, CUDA events)."""
+    import torch
+    src = torch.empty(1 << 30, dtype=torch.uint8).pin_memory()
+    dst = torch.empty(1 << 30, dtype=torch.uint8, device=dev)
+    best = float("inf")
+    for _ in range(3):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        dst.copy_(src, non_blocking=True)
+        e1.record()
+        torch.cuda.synchronize()
+        best = min(best, e0.elapsed_time(e1))
+    del src, dst
+    return (1 << 30) / (best / 1000.0) / 1e9
 
 
 def read_profile_traffic(name: str) -> float | None:
@@ -291,8 +349,13 @@ def main() -> int:
     ap.add_argument("--pipe-width", type=int, default=2)
     ap.add_argument("--early-exit", default="none", choices=["none", "gpruning"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--latency", default="",
-                    help="also time small batches end to end, e.g. 1,4,16 (latency mode; rank 0 only)")
+    ap.add_argument("--latency", default="1,4,16",
+                    help="also time small batches end to end (latency mode, the batches of config 4; rank 0 "
+                         "only); empty to skip")
+    ap.add_argument("--no-host-pages", action="store_true",
+                    help="skip the host-DRAM page store pass (host_pages object, N = 1)")
+    ap.add_argument("--no-striped", action="store_true",
+                    help="skip the shared striped page store pass (striped object, N > 1)")
     ap.add_argument("--stripe-devices", default="",
                     help="stripe the page store over these GPUs, e.g. 0,1 (pages p mod S; peer loads)")
     ap.add_argument("--page-store", default="hbm", choices=["hbm", "host"],
@@ -476,6 +539,53 @@ def main() -> int:
             latency[str(b)] = {"batches": reps, "p50_ms": float(np.percentile(times, 50)),
                                "p99_ms": float(np.percentile(times, 99)), "qps": b * 1e3 / statistics.mean(times)}
 
+    # host-DRAM page store (config 2's layout): the same step with node records read over PCIe from pinned,
+    # mapped host memory; everything else in HBM.  N = 1 only.
+    host_pages = None
+    if world == 1 and not args.no_host_pages and args.page_store == "hbm" and not stripes and not args.stripe_shared:
+        ref_ids = d_ids.clone()
+        with Engine.open(d, w.data_type, device=local, page_store="host") as eh:
+            h_ms, h_total = time_steps(eh, dq, p, d_ids, d_dists, stream, args.steps, args.warmup, barrier, dev)
+            same = bool(torch.equal(d_ids, ref_ids))
+        rec_bytes = expansions * info.node_size
+        pcie_peak = pcie_h2d_gbs(dev)
+        h_avg = statistics.mean(h_ms)
+        host_pages = {"qps": args.steps * nq / (h_total / 1000.0), "ms_per_step": h_total / args.steps,
+                      "ids_equal_to_hbm_store": same, "recall_at_10": recall if same else None,
+                      "record_bytes_per_step": rec_bytes, "pcie_gbs": rec_bytes / (h_avg / 1000.0) / 1e9,
+                      "pcie_peak_gbs": pcie_peak, "pcie_frac": rec_bytes / (h_avg / 1000.0) / 1e9 / pcie_peak,
+                      "how": "qv_search_device on the same resident queries with QV_PAGES_HOST (the page store "
+                             "in pinned host DRAM mapped into the GPU, records read by the kernel over PCIe); "
+                             "record bytes = expansions x node_size; peak = a pinned 1 GiB host-to-device copy "
+                             "timed in this run"}
+        del ref_ids
+
+    # shared striped page store (the 1B layout): rank r holds pages p = r (mod N) in its HBM and reads the
+    # other ranks' pages over NVLink with peer loads; the same per-rank step batch.  N > 1, every rank.
+    striped = None
+    if world > 1 and not args.no_striped and not args.stripe_shared and not stripes:
+        ref_ids = d_ids.clone()
+        es = shard.open_shared(d, w.data_type, device=local)
+        s_ms, s_total = time_steps(es, dq, p, d_ids, d_dists, stream, args.steps, args.warmup, barrier, dev)
+        same = torch.tensor([1 if torch.equal(d_ids, ref_ids) else 0], dtype=torch.int32, device=dev)
+        dist.all_reduce(same, op=dist.ReduceOp.MIN)
+        remote = torch.tensor([expansions * info.node_size * (world - 1) / world / (statistics.mean(s_ms) / 1000.0)],
+                              dtype=torch.float64, device=dev)
+        dist.all_reduce(remote, op=dist.ReduceOp.SUM)
+        barrier()  # every rank reads every other rank's stripe: close only when all are done
+        es.close()
+        del ref_ids
+        s_value = world * args.steps * nq / (s_total / 1000.0)
+        nvl = read_nvlink_peak()
+        per_gpu = float(remote.item()) / world / 1e9
+        striped = {"qps": s_value, "ms_per_step": s_total / args.steps, "efficiency_vs_replicated": s_value / value,
+                   "ids_equal_to_replicated": bool(same.item()), "nvlink_gbs_per_gpu": per_gpu,
+                   "nvlink_peak_gbs": nvl["gbs"], "nvlink_peak_source": nvl["source"],
+                   "nvlink_frac": per_gpu / nvl["gbs"],
+                   "how": "QV_PAGES_SHARED: page p on rank p mod N (CUDA IPC, peer loads, no multicast); remote "
+                          "record bytes = expansions x node_size x (N-1)/N per rank over its mean step time, "
+                          "averaged over ranks"}
+
     if rank == 0:
         peaks = read_peaks()
         avg_ms = statistics.mean(step_ms)
@@ -522,6 +632,10 @@ def main() -> int:
             line["roofline"]["traffic"] = None
             line["roofline"]["note"] = (f"node records ({expansions * info.node_size / 1e9:.2f} GB per launch) are read "
                                         "from pinned host DRAM over PCIe; the HBM fraction does not bound this mode")
+        if host_pages:
+            line["host_pages"] = host_pages
+        if striped:
+            line["striped"] = striped
         if latency:
             line["latency_mode"] = {"per_batch_size": latency,
                                     "how": "qv_search on pinned host buffers, host wall time per batch "

@@ -100,6 +100,7 @@ typedef struct {
   /* visited-filter mode: ids scheduled for expansion this query (open
    * addressing, id + 1, 0 = empty) */
   uint32_t* vset; int64_t vcap, vcount; int vfilter;
+  int route_exact;                            /* diagnostic: exact L2 instead of ADC */
 } orc_ctx;
 
 static uint64_t vhash(uint32_t id) { return (uint64_t)id * 0x9E3779B97F4A7C15ull; }
@@ -175,7 +176,9 @@ static int orc_merge(const orc_index* ix, orc_ctx* c, int64_t node, int ef) {
     memcpy(&nb, rec + ix->data_size + 4 + 4 * (int64_t)t, 4);
     if ((int64_t)nb >= ix->num_points) return -1;
     c->tid[sz + t] = nb;
-    c->tdist[sz + t] = orc_adc(c->lut, ix->codes + (int64_t)nb * M, M);
+    c->tdist[sz + t] = c->route_exact
+        ? orc_exact_l2(c->q2, node_record(ix, nb), ix->dim, ix->data_type)
+        : orc_adc(c->lut, ix->codes + (int64_t)nb * M, M);
   }
   c->nbrs += deg;
   if (c->vfilter) {  /* visited-filter mode: drop ids already scheduled for expansion */
@@ -451,6 +454,7 @@ static int orc_search_one(const orc_index* ix, const orc_nav* nav, orc_ctx* c, c
     if (entry < 0) return (int)entry;
   }
   c->vfilter = p->visited_filter;
+  c->route_exact = p->route_exact;
   if (c->vfilter) {
     memset(c->vset, 0, sizeof(uint32_t) * c->vcap);
     c->vcount = 0;

@@ -64,6 +64,10 @@ typedef struct {
   int32_t num_threads;          /* OpenMP threads for orc_search; <=0 means all */
   int32_t visited_filter;       /* 1: a node scheduled for expansion never re-enters the list
                                    (a mode of this build, not reference behaviour); 0: reference */
+  int32_t route_exact;          /* diagnostic, not reference behaviour: 1 scores each neighbour by
+                                   its exact L2 (orc_exact_l2 of its record's vector) instead of
+                                   ADC, so a walk of the same graph without PQ error can be compared
+                                   with the reference walk; 0: reference (ADC) */
 } orc_params;
 
 /* A navigation graph (src/shared/index/nav_graph.cu:12-73).  Vectors have

@@ -52,7 +52,8 @@ class _Index(C.Structure):
 class _Params(C.Structure):
     _fields_ = [("topk", C.c_int32), ("ef_search", C.c_int32), ("pipe_width", C.c_int32),
                 ("early_exit_policy", C.c_int32), ("gpruning_warmup_steps", C.c_int32),
-                ("gpruning_patience", C.c_int32), ("num_threads", C.c_int32), ("visited_filter", C.c_int32)]
+                ("gpruning_patience", C.c_int32), ("num_threads", C.c_int32), ("visited_filter", C.c_int32),
+                ("route_exact", C.c_int32)]
 
 
 _lib = None
@@ -251,7 +252,10 @@ def exact_l2(ix: OracleIndex, q2: np.ndarray, v: int) -> float:
 
 def search(ix: OracleIndex, queries: np.ndarray, *, topk: int = 10, ef_search: int = 30, pipe_width: int = 1,
            early_exit_policy: str = "none", gpruning_warmup_steps: int = 10, gpruning_patience: int = 8,
-           num_threads: int = 0, nav: OracleNav | None = None, visited_filter: bool = False) -> dict:
+           num_threads: int = 0, nav: OracleNav | None = None, visited_filter: bool = False,
+           route_exact: bool = False) -> dict:
+    """The reference walk (pipe lanes completing in lane order).  route_exact (diagnostic, not reference
+    behaviour) scores neighbours by exact L2 instead of ADC, to separate PQ error from graph quality."""
     q = np.ascontiguousarray(queries, dtype=np.float32)
     nq = q.shape[0]
     ids = np.empty((nq, topk), dtype=np.int32)
@@ -261,7 +265,7 @@ def search(ix: OracleIndex, queries: np.ndarray, *, topk: int = 10, ef_search: i
     nbrs = np.empty(nq, dtype=np.int64)
     pol = {"none": 0, "gpruning": 2}[early_exit_policy]
     p = _Params(topk, ef_search, pipe_width, pol, gpruning_warmup_steps, gpruning_patience, num_threads,
-                1 if visited_filter else 0)
+                1 if visited_filter else 0, 1 if route_exact else 0)
     rc = lib().orc_search_nav(C.byref(ix._c), C.byref(nav._c) if nav is not None else None, q.ctypes.data, nq,
                               C.byref(p), ids.ctypes.data, dists.ctypes.data, found.ctypes.data,
                               steps.ctypes.data, nbrs.ctypes.data)

@@ -48,6 +48,9 @@ CONFIGS = {
     # 100M x 128-d uint8 mixture as config 0 with 10K clusters, R=64, PQ 32 x 256 (3.2 GB of
     # codes, 41 GB of graph pages -- both fit one B200's HBM), 100K queries per step, top-10.
     "config2": Workload("config2", 100_000_000, 128, "uint8", 10_000, 20.0, 64, 100, 1.2, 32, 100_000, 10, 45),
+    # the first 10M rows of config 2's base stream (same 10K-cluster mixture, same query stream): config 2's
+    # data at a size that builds in minutes, for recall diagnosis
+    "config2-10m": Workload("config2-10m", 10_000_000, 128, "uint8", 10_000, 20.0, 64, 100, 1.2, 32, 10_000, 10, 45),
     # small shapes of config0 for tests and smoke runs
     "config0-100k": Workload("config0-100k", 100_000, 128, "uint8", 100, 20.0, 64, 100, 1.2, 32, 10_000, 10, 45),
     "config0-20k": Workload("config0-20k", 20_000, 128, "uint8", 20, 20.0, 64, 100, 1.2, 32, 2_000, 10, 45),

@@ -191,3 +191,23 @@ def test_uint8_exact_l2_is_integer_exact():
         x = rng.integers(0, 256, 128).astype(np.uint8)
         got = pyoracle.lib().orc_exact_l2(q.ctypes.data, x.ctypes.data, 128, 0)
         assert got == float(((q.astype(np.int64) - x.astype(np.int64)) ** 2).sum())
+
+
+def test_exact_routing_diagnostic(u8_index):
+    """The oracle's route_exact diagnostic walks the same graph with every neighbour scored by its exact L2:
+    result distances are still the exact L2 of the returned ids, and on this well-built fixture the walk
+    without PQ error finds at least as many true neighbours as the reference walk."""
+    from oracle import pyoracle
+    ix = pyoracle.load_index(u8_index["dir"], "uint8")
+    q = u8_index["queries"]
+    pq = pyoracle.search(ix, q, topk=10, ef_search=24, pipe_width=2, early_exit_policy="none")
+    ex = pyoracle.search(ix, q, topk=10, ef_search=24, pipe_width=2, early_exit_policy="none", route_exact=True)
+    base = u8_index["base"].astype(np.int64)
+    for r in range(len(q)):
+        got = ex["ids"][r][ex["ids"][r] >= 0]
+        want = ((base[got] - q[r].astype(np.int64)) ** 2).sum(1).astype(np.float32)
+        np.testing.assert_array_equal(ex["dists"][r][: len(got)], want)
+    r_pq = pyoracle.calc_recall(pq["ids"], u8_index["gt"], 10)
+    r_ex = pyoracle.calc_recall(ex["ids"], u8_index["gt"], 10)
+    assert r_ex >= r_pq
+    assert not np.array_equal(pq["ids"], ex["ids"])
