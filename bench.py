@@ -582,7 +582,7 @@ def main() -> int:
                    "ids_equal_to_replicated": bool(same.item()), "nvlink_gbs_per_gpu": per_gpu,
                    "nvlink_peak_gbs": nvl["gbs"], "nvlink_peak_source": nvl["source"],
                    "nvlink_frac": per_gpu / nvl["gbs"],
-                   "how": "QV_PAGES_SHARED: page p on rank p mod N (CUDA IPC, peer loads, no multicast); remote "
+                   "how": "QV_PAGES_SHARED: page p on rank p mod N (CUDA IPC, plain peer loads); remote "
                           "record bytes = expansions x node_size x (N-1)/N per rank over its mean step time, "
                           "averaged over ranks"}
 
