@@ -281,6 +281,53 @@ def cpu_baseline(w, d, ef: int, args, seconds: float = CPU_SAMPLE_SECONDS) -> di
             "sample": f"{rows}, ef_search={ef}, {dt:.1f} s of host work"}
 
 
+def host_pages_pass(args, w, d, local, dev, dq, p, d_ids, d_dists, stream, barrier, nq, rec_bytes, recall) -> dict:
+    """The headline step again with the page store in pinned host DRAM mapped into the GPU (QV_PAGES_HOST):
+    node records cross PCIe, everything else stays in HBM.  Same resident queries, ef and pipe width."""
+    import torch
+    from quiver_b200 import Engine
+    ref_ids = d_ids.clone()
+    with Engine.open(d, w.data_type, device=local, page_store="host") as eh:
+        h_ms, h_total = time_steps(eh, dq, p, d_ids, d_dists, stream, args.steps, args.warmup, barrier, dev)
+        same = bool(torch.equal(d_ids, ref_ids))
+    pcie_peak = pcie_h2d_gbs(dev)
+    gbs = rec_bytes / (statistics.mean(h_ms) / 1000.0) / 1e9
+    return {"qps": args.steps * nq / (h_total / 1000.0), "ms_per_step": h_total / args.steps,
+            "ids_equal_to_hbm_store": same, "recall_at_10": recall if same else None,
+            "record_bytes_per_step": rec_bytes, "pcie_gbs": gbs, "pcie_peak_gbs": pcie_peak,
+            "pcie_frac": gbs / pcie_peak,
+            "how": "qv_search_device on the same resident queries with QV_PAGES_HOST (the page store in pinned "
+                   "host DRAM mapped into the GPU, records read by the kernel over PCIe); record bytes = "
+                   "expansions x node_size; peak = a pinned 1 GiB host-to-device copy timed in this run"}
+
+
+def striped_pass(args, w, d, local, dev, dq, p, d_ids, d_dists, stream, barrier, nq, world, rec_bytes,
+                 replicated_qps) -> dict:
+    """The headline step with the page store striped over the ranks (QV_PAGES_SHARED: page p on rank p mod N,
+    opened by CUDA IPC, read with plain peer loads).  Every rank takes the same collective steps."""
+    import torch
+    import torch.distributed as dist
+    from quiver_b200 import shard
+    ref_ids = d_ids.clone()
+    es = shard.open_shared(d, w.data_type, device=local)
+    s_ms, s_total = time_steps(es, dq, p, d_ids, d_dists, stream, args.steps, args.warmup, barrier, dev)
+    same = torch.tensor([1 if torch.equal(d_ids, ref_ids) else 0], dtype=torch.int32, device=dev)
+    dist.all_reduce(same, op=dist.ReduceOp.MIN)
+    remote = torch.tensor([rec_bytes * (world - 1) / world / (statistics.mean(s_ms) / 1000.0)], dtype=torch.float64,
+                          device=dev)
+    dist.all_reduce(remote, op=dist.ReduceOp.SUM)
+    barrier()  # every rank reads every other rank's stripe: close only when all are done
+    es.close()
+    s_value = world * args.steps * nq / (s_total / 1000.0)
+    nvl = read_nvlink_peak()
+    per_gpu = float(remote.item()) / world / 1e9
+    return {"qps": s_value, "ms_per_step": s_total / args.steps, "efficiency_vs_replicated": s_value / replicated_qps,
+            "ids_equal_to_replicated": bool(same.item()), "nvlink_gbs_per_gpu": per_gpu,
+            "nvlink_peak_gbs": nvl["gbs"], "nvlink_peak_source": nvl["source"], "nvlink_frac": per_gpu / nvl["gbs"],
+            "how": "QV_PAGES_SHARED: page p on rank p mod N (CUDA IPC, plain peer loads); remote record bytes = "
+                   "expansions x node_size x (N-1)/N per rank over its mean step time, averaged over ranks"}
+
+
 ADC_POINTS, ADC_QUERIES, ADC_PER_QUERY = 100_000_000, 2048, 65_536
 # (mode, kernel, algorithmic bytes per pair): 32 code + 4 distance written, + 4 id read for gathers
 ADC_DEFAULT = (("stream", "pipe", 36), ("gather", "thread", 40))
@@ -543,48 +590,18 @@ def main() -> int:
     # mapped host memory; everything else in HBM.  N = 1 only.
     host_pages = None
     if world == 1 and not args.no_host_pages and args.page_store == "hbm" and not stripes and not args.stripe_shared:
-        ref_ids = d_ids.clone()
-        with Engine.open(d, w.data_type, device=local, page_store="host") as eh:
-            h_ms, h_total = time_steps(eh, dq, p, d_ids, d_dists, stream, args.steps, args.warmup, barrier, dev)
-            same = bool(torch.equal(d_ids, ref_ids))
-        rec_bytes = expansions * info.node_size
-        pcie_peak = pcie_h2d_gbs(dev)
-        h_avg = statistics.mean(h_ms)
-        host_pages = {"qps": args.steps * nq / (h_total / 1000.0), "ms_per_step": h_total / args.steps,
-                      "ids_equal_to_hbm_store": same, "recall_at_10": recall if same else None,
-                      "record_bytes_per_step": rec_bytes, "pcie_gbs": rec_bytes / (h_avg / 1000.0) / 1e9,
-                      "pcie_peak_gbs": pcie_peak, "pcie_frac": rec_bytes / (h_avg / 1000.0) / 1e9 / pcie_peak,
-                      "how": "qv_search_device on the same resident queries with QV_PAGES_HOST (the page store "
-                             "in pinned host DRAM mapped into the GPU, records read by the kernel over PCIe); "
-                             "record bytes = expansions x node_size; peak = a pinned 1 GiB host-to-device copy "
-                             "timed in this run"}
-        del ref_ids
+        try:
+            host_pages = host_pages_pass(args, w, d, local, dev, dq, p, d_ids, d_dists, stream, barrier, nq,
+                                         expansions * info.node_size, recall)
+        except Exception as err:  # the headline stands without it (e.g. not enough pinnable host memory)
+            host_pages = {"error": f"{type(err).__name__}: {err}"}
 
     # shared striped page store (the 1B layout): rank r holds pages p = r (mod N) in its HBM and reads the
     # other ranks' pages over NVLink with peer loads; the same per-rank step batch.  N > 1, every rank.
     striped = None
     if world > 1 and not args.no_striped and not args.stripe_shared and not stripes:
-        ref_ids = d_ids.clone()
-        es = shard.open_shared(d, w.data_type, device=local)
-        s_ms, s_total = time_steps(es, dq, p, d_ids, d_dists, stream, args.steps, args.warmup, barrier, dev)
-        same = torch.tensor([1 if torch.equal(d_ids, ref_ids) else 0], dtype=torch.int32, device=dev)
-        dist.all_reduce(same, op=dist.ReduceOp.MIN)
-        remote = torch.tensor([expansions * info.node_size * (world - 1) / world / (statistics.mean(s_ms) / 1000.0)],
-                              dtype=torch.float64, device=dev)
-        dist.all_reduce(remote, op=dist.ReduceOp.SUM)
-        barrier()  # every rank reads every other rank's stripe: close only when all are done
-        es.close()
-        del ref_ids
-        s_value = world * args.steps * nq / (s_total / 1000.0)
-        nvl = read_nvlink_peak()
-        per_gpu = float(remote.item()) / world / 1e9
-        striped = {"qps": s_value, "ms_per_step": s_total / args.steps, "efficiency_vs_replicated": s_value / value,
-                   "ids_equal_to_replicated": bool(same.item()), "nvlink_gbs_per_gpu": per_gpu,
-                   "nvlink_peak_gbs": nvl["gbs"], "nvlink_peak_source": nvl["source"],
-                   "nvlink_frac": per_gpu / nvl["gbs"],
-                   "how": "QV_PAGES_SHARED: page p on rank p mod N (CUDA IPC, plain peer loads); remote "
-                          "record bytes = expansions x node_size x (N-1)/N per rank over its mean step time, "
-                          "averaged over ranks"}
+        striped = striped_pass(args, w, d, local, dev, dq, p, d_ids, d_dists, stream, barrier, nq, world,
+                               expansions * info.node_size, value)
 
     if rank == 0:
         peaks = read_peaks()
@@ -641,7 +658,10 @@ def main() -> int:
                                     "how": "qv_search on pinned host buffers, host wall time per batch "
                                            "(H2D, one kernel, D2H, sync), same ef / pipe width"}
         if world == 1 and not args.no_cpu_baseline:
-            line["cpu_baseline"] = cpu_baseline(w, d, ef, args)
+            try:
+                line["cpu_baseline"] = cpu_baseline(w, d, ef, args)
+            except Exception as err:  # e.g. the host cannot hold a second copy of a large index
+                line["cpu_baseline"] = {"error": f"{type(err).__name__}: {err}"}
         if not args.no_adc:
             line["adc_batch"] = adc_microbench(dev, stream, peaks["hbm_gbs"])
         print(json.dumps(line), flush=True)

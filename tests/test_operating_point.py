@@ -79,7 +79,7 @@ def test_r100_large_lists(engines, odd_index, W, ef):
              early_exit_policy="gpruning")
 
 
-@pytest.mark.parametrize("ef", [513, 700, 1024])
+@pytest.mark.parametrize("ef", [513, 700, 1024, 2048, 4096])
 @pytest.mark.parametrize("W", [1, 2])
 def test_u8_per_record_merge(engines, u8_index, ef, W):
     """Lists above 512 entries: the per-record merge with the chunked shift."""
