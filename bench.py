@@ -248,6 +248,9 @@ def reference_arm(args, rank: int, world: int) -> int:
         "cpu_baseline": {"value": qps, "unit": "queries/s", "cores": cores, "kind": "port", "sample": sample},
         "e2e": {"value": qps, "unit": "queries/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "recall_at_10": recall,
+        "note": ("timed: the oracle's search only (the C restatement of the reference kernel, all host threads), "
+                 "on a bounded sample of each step's queries; the index it searches -- its input -- is built "
+                 "beforehand by this repository's GPU builder, bit-identical to the host build"),
     }
     print(json.dumps(line), flush=True)
     return 0

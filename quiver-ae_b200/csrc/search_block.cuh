@@ -455,6 +455,10 @@ __device__ __forceinline__ void merge_visit_select(const SearchParams& p, const 
   }
 
   // Long lists (ef > 512): shift in 128-entry chunks, highest first, then scan.
+  // An entry only moves up (dst >= i), so a chunk's writes never touch the
+  // lower chunks that are still to be read, and every write into a chunk's
+  // own positions -- from that chunk or a lower one -- comes after the
+  // barrier that follows the chunk's reads: one barrier per chunk.
   if (nsurv > 0) {
     const int first = s.S[0];
     if (first < sz) {
@@ -474,7 +478,6 @@ __device__ __forceinline__ void merge_visit_select(const SearchParams& p, const 
           s.lid[dst] = xid;
           s.ldist[dst] = xd;
         }
-        __syncthreads();
       }
     }
     if (tid < nsurv) {
@@ -741,8 +744,15 @@ __device__ __forceinline__ void merge_group_many(const SearchParams& p, const BS
 // When more than 32 pairs survive the filter (the opening hops of a query),
 // all threads rank them instead (merge_group_many_rank) and warp 0 takes the
 // picks from the sorted survivors.
+//
+// The caller does not wait for the group's fetch and scoring to finish in
+// every warp: phase A needs only this thread's own pair and the list (last
+// written before the previous group's final barrier), so the first barrier
+// here also publishes what the fetch wrote (degrees, nodes, exact distances,
+// the error word).  Returns false, right after that barrier, when the fetch
+// reported a device error.
 template <typename T, int RP>
-__device__ __forceinline__ void merge_group(const SearchParams& p, const BSlot& s, int gact, bool live, float d,
+__device__ __forceinline__ bool merge_group(const SearchParams& p, const BSlot& s, int gact, bool live, float d,
                                             uint32_t id) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int sz = s.misc[kMiscSize];
@@ -797,6 +807,7 @@ __device__ __forceinline__ void merge_group(const SearchParams& p, const BSlot& 
     }
   }
   __syncthreads();
+  if (s.misc[kMiscErr]) return false;  // uniform: read after the barrier
 
   unsigned m[4];
   int npre = 0;
@@ -809,7 +820,7 @@ __device__ __forceinline__ void merge_group(const SearchParams& p, const BSlot& 
   // 1 visits the records' nodes in lane order.
   if (npre > 32) {  // uniform: every thread read the same ballots
     merge_group_many<RP>(p, s, gact, sz, npre, pre, d, id);
-    return;
+    return true;
   }
   if (warp == 0) {
     int slot = -1;
@@ -924,6 +935,7 @@ __device__ __forceinline__ void merge_group(const SearchParams& p, const BSlot& 
     lc.d[x] = vd[x];
   }
   merge_group_write(p, s, gact, sz, lc);
+  return true;
 }
 
 // Expand the lanes in `mask`, in lane order, G = 128 / RP records at a time.
@@ -1001,12 +1013,12 @@ __device__ int expand_block(const SearchParams& p, const BSlot& s, uint32_t mask
         d = acc;
       }
     }
-    __syncthreads();
-    if (s.misc[kMiscErr]) return s.misc[kMiscErr];
-    if (p.ef <= kBlock * kFastEntries) {
-      merge_group<T, RP>(p, s, gact, live, d, nb);
+    if (p.ef <= kBlock * kFastEntries) {  // uniform
+      if (!merge_group<T, RP>(p, s, gact, live, d, nb)) return s.misc[kMiscErr];
       continue;
     }
+    __syncthreads();
+    if (s.misc[kMiscErr]) return s.misc[kMiscErr];
     for (int gg = 0; gg < gact; ++gg) merge_visit_select<T, RP>(p, s, gg, g == gg, live, d, nb);
   }
   return 0;
@@ -1086,6 +1098,7 @@ __device__ void run_query_block(const SearchParams& p, const BSlot& s, int64_t q
       for (int w = 1; w < p.W; ++w) select_block_warp(s, w, lane);
     __syncthreads();
     int64_t iters = 0;
+    const uint32_t all_lanes = (p.W >= 32) ? 0xffffffffu : ((1u << p.W) - 1u);
     while (!s.misc[kMiscStop]) {
       uint32_t active = 0;
       for (int w = 0; w < p.W; ++w)
@@ -1096,13 +1109,19 @@ __device__ void run_query_block(const SearchParams& p, const BSlot& s, int64_t q
         err = kErrHopCap;
         break;
       }
-      __syncthreads();  // everyone has read lane[] before it changes
+      // lane[] is next written by the merges, after at least one barrier
+      // inside expand_block, so every thread has read it by then.
       err = expand_block<T, MC, RP>(p, s, active, qid);
       if (err || s.misc[kMiscStop]) break;
-      if (warp == 0)
-        for (int w = 0; w < p.W; ++w)
-          if (!(active & (1u << w))) select_block_warp(s, w, lane);
-      __syncthreads();
+      // Idle lanes pick their next node; when every lane was active nothing
+      // is written here and the merge's final barrier already ordered the
+      // next iteration's reads.  `active` is uniform.
+      if (active != all_lanes) {
+        if (warp == 0)
+          for (int w = 0; w < p.W; ++w)
+            if (!(active & (1u << w))) select_block_warp(s, w, lane);
+        __syncthreads();
+      }
     }
   }
   for (int i = tid; i < p.k; i += kBlock) {
