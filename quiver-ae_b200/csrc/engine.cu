@@ -191,6 +191,7 @@ Plan make_plan(qv_engine* e, const qv_search_opts& o, int64_t nq) {
   Plan pl;
   const auto& L = e->L;
   set_kernel_shape(e, pl);
+  pl.long_lists = o.ef_search > qvk::kBlock * qvk::kFastEntries;
   // --queries-per-block 0/1: one query per 128-thread CTA (the block kernel);
   // Q >= 2: Q one-warp query slots per CTA (the warp kernel).  Both give
   // identical results.
@@ -416,8 +417,9 @@ void prepare_noalloc(qv_engine* e) {
   e->d_noalloc = static_cast<unsigned char*>(ptr);
   Plan pl;
   set_kernel_shape(e, pl);
-  for (const bool block : {true, false}) {
-    pl.block = block;
+  for (const int variant : {0, 1, 2}) {  // block kernel for short and long lists, warp kernel
+    pl.block = variant < 2;
+    pl.long_lists = variant == 1;
     bind_kernels(e, pl);
     cudaFuncAttributes attr;
     CK(cudaFuncGetAttributes(&attr, pl.fn));

@@ -14,6 +14,7 @@ struct Plan {
   int smax = 2;         // neighbours per lane (R <= 32 * smax)
   int mc = 0;           // PQ code width the kernel is specialised for (0 = any)
   int slots = 1;        // query slots (warps) per CTA
+  bool long_lists = false;  // block kernel: ef above 512 (the group merge's in-place path for long lists)
   int blocks_per_sm = 0;
   int grid = 0;
   int smem = 0;
@@ -36,18 +37,24 @@ void launch_search(const qvk::SearchParams& p, int grid, int block, int smem, cu
   qvk::search_kernel<T, MC, SMAX, STREAM><<<grid, block, smem, st>>>(p);
 }
 
-template <typename T, int MC, int RP, bool STREAM>
+template <typename T, int MC, int RP, bool STREAM, bool LONG>
 void launch_block(const qvk::SearchParams& p, int grid, int block, int smem, cudaStream_t st) {
-  qvk::search_block_kernel<T, MC, RP, STREAM><<<grid, block, smem, st>>>(p);
+  qvk::search_block_kernel<T, MC, RP, STREAM, LONG><<<grid, block, smem, st>>>(p);
+}
+
+template <typename T, int MC, int RP, bool LONG>
+void bind_block(Plan& pl) {
+  pl.fn = reinterpret_cast<const void*>(&qvk::search_block_kernel<T, MC, RP, false, LONG>);
+  pl.launch = &launch_block<T, MC, RP, false, LONG>;
+  pl.fn_stream = reinterpret_cast<const void*>(&qvk::search_block_kernel<T, MC, RP, true, LONG>);
+  pl.launch_stream = &launch_block<T, MC, RP, true, LONG>;
 }
 
 template <typename T, int MC, int SMAX>
 void bind_one(Plan& pl) {
   if (pl.block) {
-    pl.fn = reinterpret_cast<const void*>(&qvk::search_block_kernel<T, MC, 32 * SMAX, false>);
-    pl.launch = &launch_block<T, MC, 32 * SMAX, false>;
-    pl.fn_stream = reinterpret_cast<const void*>(&qvk::search_block_kernel<T, MC, 32 * SMAX, true>);
-    pl.launch_stream = &launch_block<T, MC, 32 * SMAX, true>;
+    if (pl.long_lists) bind_block<T, MC, 32 * SMAX, true>(pl);
+    else bind_block<T, MC, 32 * SMAX, false>(pl);
   } else {
     pl.fn = reinterpret_cast<const void*>(&qvk::search_kernel<T, MC, SMAX, false>);
     pl.launch = &launch_search<T, MC, SMAX, false>;

@@ -6,24 +6,21 @@
 // work of a hop is spread over four warps:
 //   fetch + ADC   one neighbour per thread; a group of 128 / RP pipe lanes
 //                 (RP = R rounded up to 64 or 128) is fetched and scored at
-//                 once, so their node-record and code gathers overlap; each
-//                 warp sorts its 32 pairs, and the runs of a record are
-//                 merged by binary search into one sorted array per record;
-//   merge         per record, in lane order: every new pair binary-searches
-//                 its insertion point in the list; a pair whose id is in the
-//                 list or repeats an earlier pair's id is dropped
-//                 (kernel_helpers.cuh:331-335 places it right after its twin
-//                 and :440-455 removes it); survivors get their final
-//                 positions from a block prefix count; old entries move up by
-//                 the survivors inserted before them; entries pushed past ef
-//                 are discarded;
-//   visit         warp 3 scores the expanded node exactly, updates the top-k
-//                 and runs gpruning while the other warps search;
-//   select        the first unvisited entry of the merged list is either the
-//                 first survivor or the first unvisited old entry at or after
-//                 a lower bound (all entries before it are visited), so it is
-//                 known before the merged list is written: its writer sets the
-//                 visited bit.  Three barriers per expanded node.
+//                 once, so their node-record and code gathers overlap; the
+//                 last warp of each record scores its node exactly under the
+//                 code gathers;
+//   group merge   the group's records are merged into the list in one pass
+//                 (merge_group): every new pair filters itself against a full
+//                 list's last entry and binary-searches its insertion point,
+//                 dropping out when its id is listed; warp 0 ranks the
+//                 survivors and computes each lane's next pick from the
+//                 insertion points alone, while warp 1 visits the records'
+//                 nodes (top-k, gpruning); then old entries move up by the
+//                 survivors inserted before them, survivors land, entries
+//                 pushed past ef are dropped and the picks are marked visited.
+//                 Lists of up to 512 entries are moved from registers, longer
+//                 ones in place chunk by chunk.  Three barriers per group (plus
+//                 one per moved chunk of a long list).
 #pragma once
 
 #include "search_kernel.cuh"
@@ -31,7 +28,7 @@
 namespace qvk {
 
 constexpr int kBlock = 128;
-constexpr int kFastEntries = 4;   // list entries per thread held in registers (ef <= 512)
+constexpr int kFastEntries = 4;   // list entries per thread held in registers (lists of up to 512)
 
 // block scalars (misc[])
 enum : int {
@@ -45,10 +42,6 @@ enum : int {
   kMiscDeg = 12,    // [4] degree of each record of the group
   kMiscNode = 16,   // [4] node of each record of the group
   kMiscWs = 20,     // [4] lane of each record of the group
-  kMiscFu = 24,     // [4] per-warp first unvisited old entry at or after the hint
-  kMiscMask = 28,   // [4] per-warp survivor ballots
-  kMiscTwin = 32,   // 1 when a new pair repeats an earlier new pair's id
-  kMiscTwinMask = 36,  // [4] per-warp ballots of such repeats
   kMiscStep = 40,
   kMiscCnt = 41,
   kMiscLastFc = 42,
@@ -278,226 +271,6 @@ __device__ __forceinline__ void visit_warp(const SearchParams& p, const BSlot& s
   }
 }
 
-// Merge record gg of the current group into the list, visit its node, and
-// select the lane's next node.  (d, id) is this thread's new pair when it
-// owns one of record gg's neighbours (owner), else ignored.
-template <typename T, int RP>
-__device__ __forceinline__ void merge_visit_select(const SearchParams& p, const BSlot& s, int gg, bool owner,
-                                                   bool live, float d, uint32_t id) {
-  constexpr int NW = RP / 32;  // warps that hold one record's pairs
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int e = tid % RP;
-  const int sz = s.misc[kMiscSize];
-  const int h = s.misc[kMiscHint];
-  const int deg = s.misc[kMiscDeg + gg];
-  const int node = s.misc[kMiscNode + gg];
-  const int w = s.misc[kMiscWs + gg];
-  const int vwarp = (kBlock / RP == 2 && gg == 1) ? 0 : 3;  // a warp that owns none of this record's pairs
-  float* kd = s.sd;    // [RP] this record's pairs by neighbour slot
-  uint32_t* ki = s.si;
-  const bool fast = sz <= kBlock * kFastEntries;
-
-  // Phase A: pairs worse than the last entry of a full list cannot enter it;
-  // the others find their insertion point and drop out when their id is
-  // already listed.  Old entries are read, the node is visited.
-  bool surv = false;
-  int r = 0;
-  if (owner && live) {
-    bool cand = true;
-    if (sz == p.ef) cand = key_less(d, id, s.ldist[sz - 1], s.lid[sz - 1]);
-    if (cand) {
-      r = lower_bound_s(s.ldist, s.lid, sz, d, id);
-      surv = !(r < sz && ((s.lid[r] ^ id) & kIdMask) == 0);
-      if (surv && p.visited)
-        surv = !visited_has(visited_table(p, blockIdx.x), p.visited_cap, p.visited_tag0 + s.misc[kMiscQid], id);
-    }
-    kd[e] = d;
-    ki[e] = id;
-  }
-  const unsigned bal = __ballot_sync(kFull, surv);
-  uint32_t vid[kFastEntries];
-  float vd[kFastEntries];
-  int fu = 0x7fffffff;
-  if (fast) {
-#pragma unroll
-    for (int x = 0; x < kFastEntries; ++x) {
-      const int i = tid + kBlock * x;
-      vid[x] = 0;
-      vd[x] = 0.f;
-      if (i < sz) {
-        vid[x] = s.lid[i];
-        vd[x] = s.ldist[i];
-        if (i >= h && (vid[x] & kVisited) == 0) fu = min(fu, i);
-      }
-    }
-    fu = __reduce_min_sync(kFull, fu);
-  }
-  if (lane == 0) {
-    s.misc[kMiscMask + warp] = static_cast<int>(bal);
-    s.misc[kMiscFu + warp] = fu;
-  }
-  if (warp == vwarp) visit_warp(p, s, __int_as_float(s.misc[kMiscDx + gg]), node, deg, lane);
-  __syncthreads();
-
-  // Phase B: survivors rank themselves among the survivors (ties, which only
-  // a repeated id produces, by neighbour slot).  A pair repeating an earlier
-  // survivor's id marks itself; when any does, the ranks are redone without
-  // them, so only the first copy enters (the reference's compaction keeps
-  // one of adjacent equal ids).
-  unsigned masks[NW];
-  int nsurv = 0;
-#pragma unroll
-  for (int x = 0; x < NW; ++x) {
-    masks[x] = static_cast<unsigned>(s.misc[kMiscMask + gg * NW + x]);
-    nsurv += __popc(masks[x]);
-  }
-  fu = 0x7fffffff;
-#pragma unroll
-  for (int x = 0; x < 4; ++x) fu = min(fu, s.misc[kMiscFu + x]);
-  if (surv) {
-    int rank = 0;
-    bool twin = false;
-#pragma unroll
-    for (int x = 0; x < NW; ++x) {
-      unsigned m = masks[x];
-      while (m) {
-        const int u = x * 32 + __ffs(m) - 1;
-        m &= m - 1;
-        if (u == e) continue;
-        const float du = kd[u];
-        const uint32_t iu = ki[u];
-        if (key_less(du, iu, d, id)) {
-          ++rank;
-        } else if (!key_less(d, id, du, iu) && u < e) {
-          ++rank;
-          twin = true;
-        }
-      }
-    }
-    s.S[rank] = r;
-    s.fsrc[rank] = e;
-    if (twin) {
-      s.misc[kMiscTwin] = 1;
-      atomicOr(reinterpret_cast<unsigned*>(&s.misc[kMiscTwinMask + (e >> 5)]), 1u << (e & 31));
-    }
-  }
-  __syncthreads();
-  if (s.misc[kMiscTwin]) {  // rare: an adjacency list repeats an id
-#pragma unroll
-    for (int x = 0; x < NW; ++x) masks[x] &= ~static_cast<unsigned>(s.misc[kMiscTwinMask + x]);
-    const bool keep = surv && !((static_cast<unsigned>(s.misc[kMiscTwinMask + (e >> 5)]) >> (e & 31)) & 1u);
-    nsurv = 0;
-#pragma unroll
-    for (int x = 0; x < NW; ++x) nsurv += __popc(masks[x]);
-    __syncthreads();
-    if (keep) {
-      int rank = 0;
-#pragma unroll
-      for (int x = 0; x < NW; ++x) {
-        unsigned m = masks[x];
-        while (m) {
-          const int u = x * 32 + __ffs(m) - 1;
-          m &= m - 1;
-          if (u != e && key_less(kd[u], ki[u], d, id)) ++rank;
-        }
-      }
-      s.S[rank] = r;
-      s.fsrc[rank] = e;
-    }
-    surv = keep;
-    __syncthreads();
-    if (tid == 0) {
-      s.misc[kMiscTwin] = 0;
-#pragma unroll
-      for (int x = 0; x < NW; ++x) s.misc[kMiscTwinMask + x] = 0;
-    }
-  }
-
-  const int nsize = min(sz + nsurv, p.ef);
-  const bool stopped = s.misc[kMiscStop] != 0;
-  if (fast) {
-    // Phase C: shifted writes; the writer of the first unvisited entry marks it.
-    const int first = nsurv > 0 ? s.S[0] : 0x7fffffff;
-    int sel = 0x7fffffff;
-    if (nsurv > 0) sel = first;  // survivor 0 lands at S[0] + 0
-    if (fu != 0x7fffffff) sel = min(sel, fu + count_le(s.S, nsurv, fu));
-    if (sel >= nsize) sel = -1;
-#pragma unroll
-    for (int x = 0; x < kFastEntries; ++x) {
-      const int i = tid + kBlock * x;
-      if (i < sz) {
-        const int dst = i >= first ? i + count_le(s.S, nsurv, i) : i;
-        const bool mark = dst == sel;
-        if (dst < p.ef && (dst != i || mark)) {
-          s.lid[dst] = vid[x] | (mark ? kVisited : 0u);
-          s.ldist[dst] = vd[x];
-        }
-        if (mark && !stopped) s.lane[w] = static_cast<int32_t>(vid[x] & kIdMask);
-      }
-    }
-    if (tid < nsurv) {
-      const int fp = s.S[tid] + tid;
-      if (fp < p.ef) {
-        const int src = s.fsrc[tid];
-        const bool mark = fp == sel;
-        s.lid[fp] = ki[src] | (mark ? kVisited : 0u);
-        s.ldist[fp] = kd[src];
-        if (mark && !stopped) s.lane[w] = static_cast<int32_t>(ki[src]);
-      }
-    }
-    if (tid == 0) {
-      s.misc[kMiscSize] = nsize;
-      s.misc[kMiscHint] = sel >= 0 ? sel + 1 : nsize;
-      if (sel < 0 || stopped) s.lane[w] = -1;
-    }
-    __syncthreads();
-    return;
-  }
-
-  // Long lists (ef > 512): shift in 128-entry chunks, highest first, then scan.
-  // An entry only moves up (dst >= i), so a chunk's writes never touch the
-  // lower chunks that are still to be read, and every write into a chunk's
-  // own positions -- from that chunk or a lower one -- comes after the
-  // barrier that follows the chunk's reads: one barrier per chunk.
-  if (nsurv > 0) {
-    const int first = s.S[0];
-    if (first < sz) {
-      for (int cb = ((sz - 1) / kBlock) * kBlock; cb >= (first / kBlock) * kBlock; cb -= kBlock) {
-        const int i = cb + tid;
-        const bool mv = i >= first && i < sz;
-        uint32_t xid = 0;
-        float xd = 0.f;
-        int dst = 0;
-        if (mv) {
-          xid = s.lid[i];
-          xd = s.ldist[i];
-          dst = i + count_le(s.S, nsurv, i);
-        }
-        __syncthreads();
-        if (mv && dst < p.ef) {
-          s.lid[dst] = xid;
-          s.ldist[dst] = xd;
-        }
-      }
-    }
-    if (tid < nsurv) {
-      const int fp = s.S[tid] + tid;
-      if (fp < p.ef) {
-        const int src = s.fsrc[tid];
-        s.lid[fp] = ki[src];
-        s.ldist[fp] = kd[src];
-      }
-    }
-    if (tid == 0) {
-      s.misc[kMiscSize] = nsize;
-      s.misc[kMiscHint] = min(min(h + count_le(s.S, nsurv, h), first), nsize);
-    }
-    __syncthreads();
-  }
-  if (warp == 0) select_block_warp(s, w, lane);
-  __syncthreads();
-}
-
 // Position (0-based) of the n-th set bit of m; n < popc(m).
 __device__ __forceinline__ int nth_set_bit(unsigned m, int n) {
   int pos = 0;
@@ -692,6 +465,67 @@ __device__ __forceinline__ void merge_group_write(const SearchParams& p, const B
   __syncthreads();
 }
 
+// The write phase for lists longer than the registers hold (more than 512
+// entries): the same moves as merge_group_write, done in place in 128-entry
+// chunks from the highest down to the one holding the first insertion point.
+// An entry only moves up, so a chunk's writes never touch the lower chunks
+// still to be read, and every write into a chunk's positions comes after the
+// barrier that follows that chunk's reads: one barrier per chunk.  Picks are
+// marked by whoever writes their final position; a pick that is an old entry
+// before the first insertion point does not move and is marked in place.
+__device__ __forceinline__ void merge_group_write_long(const SearchParams& p, const BSlot& s, int gact, int sz) {
+  const int tid = threadIdx.x;
+  const int ef = p.ef;
+  const int ns = s.misc[kMiscGNs];
+  const int pos0 = s.misc[kMiscGPos0];
+  const int pos1 = s.misc[kMiscGPos1];
+  const int first = ns > 0 ? s.S[0] : 0x7fffffff;
+  if (first < sz) {
+    for (int cb = ((sz - 1) / kBlock) * kBlock; cb >= (first / kBlock) * kBlock; cb -= kBlock) {
+      const int i = cb + tid;
+      const bool mv = i >= first && i < sz;
+      uint32_t xid = 0;
+      float xd = 0.f;
+      int dst = 0;
+      if (mv) {
+        xid = s.lid[i];
+        xd = s.ldist[i];
+        dst = i + count_le(s.S, ns, i);
+      }
+      __syncthreads();
+      if (mv && dst < ef) {
+        const bool mark = dst == pos0 || dst == pos1;
+        s.lid[dst] = xid | (mark ? kVisited : 0u);
+        s.ldist[dst] = xd;
+      }
+    }
+  }
+  if (tid < ns) {
+    const int fp = s.S[tid] + tid;
+    const int src = s.fsrc[tid];
+    if (fp >= 0 && fp < ef && src >= 0 && src < kBlock) {
+      const bool mark = fp == pos0 || fp == pos1;
+      s.lid[fp] = s.si[src] | (mark ? kVisited : 0u);
+      s.ldist[fp] = s.sd[src];
+    }
+  }
+  if (tid == 0) {
+    // survivors land at or after `first` and moved entries above it, so
+    // positions below it still hold their old, unmoved entries
+    if (pos0 >= 0 && pos0 < first && pos0 < sz) s.lid[pos0] |= kVisited;
+    if (pos1 >= 0 && pos1 < first && pos1 < sz) s.lid[pos1] |= kVisited;
+    s.misc[kMiscSize] = min(sz + ns, ef);
+    s.misc[kMiscHint] = s.misc[kMiscGHint];
+    const int id0 = s.misc[kMiscGId0];
+    s.lane[s.misc[kMiscWs]] = (id0 >= 0 && !s.misc[kMiscGStop0]) ? id0 : -1;
+    if (gact == 2) {
+      const int id1 = s.misc[kMiscGId1];
+      s.lane[s.misc[kMiscWs + 1]] = (id1 >= 0 && !s.misc[kMiscStop]) ? id1 : -1;
+    }
+  }
+  __syncthreads();
+}
+
 // Warp 1: visit the group's nodes in lane order, keeping the stop flag right
 // after the first visit for the first lane.
 __device__ __forceinline__ void merge_group_visits(const SearchParams& p, const BSlot& s, int gact, int lane) {
@@ -709,20 +543,25 @@ __device__ __forceinline__ void merge_group_visits(const SearchParams& p, const 
 // warp 1, then the write phase.
 template <int RP>
 __device__ __forceinline__ void merge_group_many(const SearchParams& p, const BSlot& s, int gact, int sz, int npre,
-                                                 bool pre, float d, uint32_t id) {
+                                                 bool pre, float d, uint32_t id, bool long_list) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   merge_group_many_rank<RP>(s, npre, pre, d, id);
   ListCopy lc;
+  if (!long_list) {
 #pragma unroll
-  for (int x = 0; x < kFastEntries; ++x) {
-    const int i = tid + kBlock * x;
-    lc.id[x] = i < sz ? s.lid[i] : 0u;
-    lc.d[x] = i < sz ? s.ldist[i] : 0.f;
+    for (int x = 0; x < kFastEntries; ++x) {
+      const int i = tid + kBlock * x;
+      lc.id[x] = i < sz ? s.lid[i] : 0u;
+      lc.d[x] = i < sz ? s.ldist[i] : 0.f;
+    }
   }
   if (warp == 0) merge_group_picks_sorted<RP>(p, s, gact, sz);
   if (warp == 1) merge_group_visits(p, s, gact, lane);
   __syncthreads();
-  merge_group_write(p, s, gact, sz, lc);
+  if (long_list)
+    merge_group_write_long(p, s, gact, sz);
+  else
+    merge_group_write(p, s, gact, sz, lc);
 }
 
 // Merge the records of one group (one or two pipe lanes, in lane order) into
@@ -751,7 +590,7 @@ __device__ __forceinline__ void merge_group_many(const SearchParams& p, const BS
 // here also publishes what the fetch wrote (degrees, nodes, exact distances,
 // the error word).  Returns false, right after that barrier, when the fetch
 // reported a device error.
-template <typename T, int RP>
+template <typename T, int RP, bool LONG>
 __device__ __forceinline__ bool merge_group(const SearchParams& p, const BSlot& s, int gact, bool live, float d,
                                             uint32_t id) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -780,21 +619,40 @@ __device__ __forceinline__ bool merge_group(const SearchParams& p, const BSlot& 
     }
   }
   const unsigned bal = __ballot_sync(kFull, pre);
+  // uniform: sz was read after a barrier; kernels for ef <= 512 compile without the long path
+  const bool long_list = LONG && sz > kBlock * kFastEntries;
   uint32_t vid[kFastEntries];
   float vd[kFastEntries];
   int f1 = 0x7fffffff, f2 = 0x7fffffff;
+  if (!long_list) {
 #pragma unroll
-  for (int x = 0; x < kFastEntries; ++x) {
-    const int i = tid + kBlock * x;
-    vid[x] = 0;
-    vd[x] = 0.f;
-    if (i < sz) {
-      vid[x] = s.lid[i];
-      vd[x] = s.ldist[i];
-      if (i >= h && (vid[x] & kVisited) == 0) {
-        if (f1 == 0x7fffffff) f1 = i; else if (f2 == 0x7fffffff) f2 = i;
+    for (int x = 0; x < kFastEntries; ++x) {
+      const int i = tid + kBlock * x;
+      vid[x] = 0;
+      vd[x] = 0.f;
+      if (i < sz) {
+        vid[x] = s.lid[i];
+        vd[x] = s.ldist[i];
+        if (i >= h && (vid[x] & kVisited) == 0) {
+          if (f1 == 0x7fffffff) f1 = i; else if (f2 == 0x7fffffff) f2 = i;
+        }
       }
     }
+  } else if (warp == 0) {
+    // the list stays in shared memory (merge_group_write_long moves it); warp 0
+    // finds the first two unvisited entries at or after the hint in 32-entry
+    // windows (entries before the hint are all visited, so this is short)
+    for (int b = h; b < sz && f2 == 0x7fffffff; b += 32) {
+      const int i = b + lane;
+      unsigned m = __ballot_sync(kFull, i < sz && (s.lid[i] & kVisited) == 0);
+      if (m && f1 == 0x7fffffff) {
+        f1 = b + __ffs(m) - 1;
+        m &= m - 1;
+      }
+      if (m) f2 = b + __ffs(m) - 1;
+    }
+    f2 = lane == 0 ? f2 : 0x7fffffff;  // lane 0 alone carries the pair into the reduction below
+    f1 = lane == 0 ? f1 : 0x7fffffff;
   }
   {
     const int w1 = __reduce_min_sync(kFull, f1);
@@ -819,7 +677,7 @@ __device__ __forceinline__ bool merge_group(const SearchParams& p, const BSlot& 
   // Phase B: warp 0 ranks the surviving pairs and computes both picks; warp
   // 1 visits the records' nodes in lane order.
   if (npre > 32) {  // uniform: every thread read the same ballots
-    merge_group_many<RP>(p, s, gact, sz, npre, pre, d, id);
+    merge_group_many<RP>(p, s, gact, sz, npre, pre, d, id, long_list);
     return true;
   }
   if (warp == 0) {
@@ -928,6 +786,10 @@ __device__ __forceinline__ bool merge_group(const SearchParams& p, const BSlot& 
   }
   __syncthreads();
 
+  if (long_list) {
+    merge_group_write_long(p, s, gact, sz);
+    return true;
+  }
   ListCopy lc;
 #pragma unroll
   for (int x = 0; x < kFastEntries; ++x) {
@@ -939,7 +801,7 @@ __device__ __forceinline__ bool merge_group(const SearchParams& p, const BSlot& 
 }
 
 // Expand the lanes in `mask`, in lane order, G = 128 / RP records at a time.
-template <typename T, int MC, int RP>
+template <typename T, int MC, int RP, bool LONG>
 __device__ int expand_block(const SearchParams& p, const BSlot& s, uint32_t mask, int64_t qid) {
   constexpr int G = kBlock / RP;
   constexpr int NV = MC > 0 ? MC / 16 : 1;
@@ -1013,13 +875,7 @@ __device__ int expand_block(const SearchParams& p, const BSlot& s, uint32_t mask
         d = acc;
       }
     }
-    if (p.ef <= kBlock * kFastEntries) {  // uniform
-      if (!merge_group<T, RP>(p, s, gact, live, d, nb)) return s.misc[kMiscErr];
-      continue;
-    }
-    __syncthreads();
-    if (s.misc[kMiscErr]) return s.misc[kMiscErr];
-    for (int gg = 0; gg < gact; ++gg) merge_visit_select<T, RP>(p, s, gg, g == gg, live, d, nb);
+    if (!merge_group<T, RP, LONG>(p, s, gact, live, d, nb)) return s.misc[kMiscErr];
   }
   return 0;
 }
@@ -1074,7 +930,7 @@ __device__ int32_t nav_entry_block(const SearchParams& p, const BSlot& s, const 
   return entry;
 }
 
-template <typename T, int MC, int RP>
+template <typename T, int MC, int RP, bool LONG>
 __device__ void run_query_block(const SearchParams& p, const BSlot& s, int64_t qid) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   if (p.out_time && tid == 0) p.out_time[2 * qid] = globaltimer_ns();
@@ -1090,7 +946,7 @@ __device__ void run_query_block(const SearchParams& p, const BSlot& s, int64_t q
   if (tid == kMiscLastTop1 || tid == kMiscLastTopk) s.misc[tid] = 0x7f800000;  // +inf
   __syncthreads();
 
-  int err = entry < 0 ? static_cast<int>(kErrNav) : expand_block<T, MC, RP>(p, s, 1u, qid);  // boot: lane 0
+  int err = entry < 0 ? static_cast<int>(kErrNav) : expand_block<T, MC, RP, LONG>(p, s, 1u, qid);  // boot: lane 0
   if (!err) {
     // lanes 1..W-1 are seeded whether or not the boot hop stopped the query
     // (kernel_q1.cuh:367-371); their picks matter only when it did not
@@ -1111,7 +967,7 @@ __device__ void run_query_block(const SearchParams& p, const BSlot& s, int64_t q
       }
       // lane[] is next written by the merges, after at least one barrier
       // inside expand_block, so every thread has read it by then.
-      err = expand_block<T, MC, RP>(p, s, active, qid);
+      err = expand_block<T, MC, RP, LONG>(p, s, active, qid);
       if (err || s.misc[kMiscStop]) break;
       // Idle lanes pick their next node; when every lane was active nothing
       // is written here and the merge's final barrier already ordered the
@@ -1141,8 +997,9 @@ __device__ void run_query_block(const SearchParams& p, const BSlot& s, int64_t q
 
 // STREAM: queries arrive while the kernel runs (streaming admission: wait for
 // each query's feed, publish completions); otherwise every query is present at
-// launch and the loop carries no streaming code.
-template <typename T, int MC, int RP, bool STREAM>
+// launch and the loop carries no streaming code.  LONG: ef may exceed 512, so
+// the group merge also carries the in-place path for long lists.
+template <typename T, int MC, int RP, bool STREAM, bool LONG>
 __global__ void __launch_bounds__(kBlock, 5) search_block_kernel(const SearchParams p) {
   extern __shared__ __align__(16) uint8_t smem[];
   const BSlot s = make_bslot(smem, p.lay);
@@ -1158,7 +1015,7 @@ __global__ void __launch_bounds__(kBlock, 5) search_block_kernel(const SearchPar
     const int qid = s.misc[kMiscQid];
     __syncthreads();
     if (qid >= p.nq) break;
-    run_query_block<T, MC, RP>(p, s, qid);
+    run_query_block<T, MC, RP, LONG>(p, s, qid);
     if constexpr (STREAM)
       if (threadIdx.x == 0) mark_done(p, blockIdx.x, ++done);
   }
