@@ -307,15 +307,42 @@ def host_pages_pass(args, w, d, local, dev, dq, p, d_ids, d_dists, stream, barri
 def striped_pass(args, w, d, local, dev, dq, p, d_ids, d_dists, stream, barrier, nq, world, rec_bytes,
                  replicated_qps) -> dict:
     """The headline step with the page store striped over the ranks (QV_PAGES_SHARED: page p on rank p mod N,
-    opened by CUDA IPC, read with plain peer loads).  Every rank takes the same collective steps."""
+    opened by CUDA IPC, read with plain peer loads).  Every rank takes the same collective steps, failures
+    included: each local step (open this rank's stripe, attach the others) is followed by an all-reduce of
+    its success, so a rank that fails makes every rank skip the rest instead of leaving the others blocked,
+    and the headline line is kept with an `error` here."""
     import torch
     import torch.distributed as dist
-    from quiver_b200 import shard
+    from quiver_b200 import Engine, shard
+
+    def all_ok(ok: bool) -> bool:
+        t = torch.tensor([1 if ok else 0], dtype=torch.int32, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MIN)
+        return bool(t.item())
+
     ref_ids = d_ids.clone()
-    es = shard.open_shared(d, w.data_type, device=local)
+    es, err = None, None
+    try:
+        es = Engine.open(d, w.data_type, device=local, page_store="shared", num_stripes=world,
+                         stripe_rank=dist.get_rank())
+    except Exception as e:  # noqa: BLE001 -- reported in the line
+        err = f"open: {type(e).__name__}: {e}"
+    if not all_ok(es is not None):
+        if es is not None:
+            es.close()
+        return {"error": err or "another rank could not open its stripe"}
+    handles = shard.exchange_stripe_handles(es.stripe_handle())
+    try:
+        es.attach_stripes(handles)
+        attached = True
+    except Exception as e:  # noqa: BLE001
+        err, attached = f"attach: {type(e).__name__}: {e}", False
+    if not all_ok(attached):
+        barrier()
+        es.close()
+        return {"error": err or "another rank could not attach the stripes"}
     s_ms, s_total = time_steps(es, dq, p, d_ids, d_dists, stream, args.steps, args.warmup, barrier, dev)
-    same = torch.tensor([1 if torch.equal(d_ids, ref_ids) else 0], dtype=torch.int32, device=dev)
-    dist.all_reduce(same, op=dist.ReduceOp.MIN)
+    same = all_ok(bool(torch.equal(d_ids, ref_ids)))
     remote = torch.tensor([rec_bytes * (world - 1) / world / (statistics.mean(s_ms) / 1000.0)], dtype=torch.float64,
                           device=dev)
     dist.all_reduce(remote, op=dist.ReduceOp.SUM)
@@ -325,7 +352,7 @@ def striped_pass(args, w, d, local, dev, dq, p, d_ids, d_dists, stream, barrier,
     nvl = read_nvlink_peak()
     per_gpu = float(remote.item()) / world / 1e9
     return {"qps": s_value, "ms_per_step": s_total / args.steps, "efficiency_vs_replicated": s_value / replicated_qps,
-            "ids_equal_to_replicated": bool(same.item()), "nvlink_gbs_per_gpu": per_gpu,
+            "ids_equal_to_replicated": same, "nvlink_gbs_per_gpu": per_gpu,
             "nvlink_peak_gbs": nvl["gbs"], "nvlink_peak_source": nvl["source"], "nvlink_frac": per_gpu / nvl["gbs"],
             "how": "QV_PAGES_SHARED: page p on rank p mod N (CUDA IPC, plain peer loads); remote record bytes = "
                    "expansions x node_size x (N-1)/N per rank over its mean step time, averaged over ranks"}
