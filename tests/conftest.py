@@ -53,6 +53,27 @@ def f32_index(tmp_path_factory):
 
 
 @pytest.fixture(scope="session")
+def i8_index(tmp_path_factory):
+    """Signed 8-bit vectors (96-d, R=64, M=32), the reference's int8 element type (.i8bin): a seeded
+    12-cluster mixture drawn with numpy (the synthetic generator makes uint8 and float only)."""
+    from quiver_b200 import builder, formats
+    rng = np.random.default_rng(15)
+    centers = rng.integers(-100, 100, size=(12, 96))
+
+    def draw(n):
+        x = centers[rng.integers(0, 12, n)] + rng.normal(0.0, 18.0, (n, 96))
+        return np.clip(np.rint(x), -128, 127).astype(np.int8)
+
+    base, queries = draw(4000), draw(64)
+    d = tmp_path_factory.mktemp("idx") / "i8"
+    builder.build_index(d, base, R=64, L=64, alpha=1.2, M=32, passes=2, pq_sample=4000, seed=15)
+    gt, _ = builder.ground_truth(base, queries, 10)
+    formats.write_bin(d / "queries.i8bin", queries)
+    formats.write_bin(d / "gt.ibin", gt)
+    return {"dir": d, "dtype": "int8", "base": base, "queries": queries.astype(np.float32), "gt": gt}
+
+
+@pytest.fixture(scope="session")
 def odd_index(tmp_path_factory):
     """Uncommon shapes: R=100 (>64 neighbours per node), M=12 (generic code path), dim=48."""
     return _make_index(tmp_path_factory.mktemp("idx"), "odd", n=2500, dim=48, dtype="uint8", centers=6,

@@ -87,6 +87,28 @@ def test_u8_per_record_merge(engines, u8_index, ef, W):
              early_exit_policy="none")
 
 
+@pytest.mark.parametrize("W", [1, 2, 4])
+@pytest.mark.parametrize("ef", [45, 320, 1024])
+@pytest.mark.parametrize("slots", [0, 2])
+def test_int8_parity(i8_index, W, ef, slots):
+    """Signed 8-bit data (the int8 instantiations of both kernels): exact distances of signed bytes, from
+    short lists to lists above 512 entries."""
+    from quiver_b200 import Engine
+    with Engine.open(i8_index["dir"], "int8", validate=True) as eng:
+        ids, _ = _compare(eng, _oracle(i8_index), i8_index["queries"], topk=10, ef_search=ef, pipe_width=W,
+                          early_exit_policy="none", queries_per_block=slots)
+    if ef >= 320:
+        from oracle import pyoracle
+        assert pyoracle.calc_recall(ids, i8_index["gt"], 10) > 0.9
+
+
+@pytest.mark.parametrize("ef", [700, 1024])
+def test_warp_kernel_long_lists(engines, u8_index, ef):
+    """The one-warp-per-query kernel with lists above 512 entries."""
+    _compare(engines["u8"], _oracle(u8_index), u8_index["queries"][:48], topk=10, ef_search=ef, pipe_width=2,
+             early_exit_policy="none", queries_per_block=2)
+
+
 @pytest.mark.parametrize("slots", [2, 4])
 def test_warp_kernel_at_operating_point(engines, u8_index, slots):
     """The one-warp-per-query kernel (queries_per_block >= 2) at ef 320 against the oracle."""
