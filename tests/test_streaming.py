@@ -115,3 +115,15 @@ def test_stream_with_visited_filter_and_nav_off(u8_index):
         _check_stream(eng, _queries(u8_index, 1500),
                       SearchParams(topk=10, ef_search=48, pipe_width=2, visited_filter=True,
                                    early_exit_policy="none"), prefeed=0, admit_min_batch=16)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("ef", [320, 700])
+def test_stream_long_lists(u8_index, ef):
+    """Streaming at the benchmark's ef and with lists above 512 entries (the long-list kernel's streaming
+    instantiation) equals the batch search."""
+    from quiver_b200 import Engine, SearchParams
+    with Engine.open(u8_index["dir"], "uint8") as eng:
+        _check_stream(eng, _queries(u8_index, 1200), SearchParams(topk=10, ef_search=ef, pipe_width=2,
+                                                                  early_exit_policy="none"),
+                      prefeed=0, admit_min_batch=16)
