@@ -38,9 +38,10 @@ sys.path.insert(0, str(ROOT / "quiver-ae_b200"))
 sys.path.insert(0, str(ROOT))
 
 METRIC = "QPS at Recall@10=0.90 and P99 latency (ms), 1/2/4/8 B200, 1B×128 uint8"
-# ef_search values tried in order; the engine accepts up to 4096 (lists above 512 entries merge record by record)
-EF_LADDER = (45, 60, 80, 100, 120, 150, 180, 220, 260, 320, 400, 512, 640, 800, 1024, 1280, 1600, 2048, 2560,
-             3200, 4096)
+# ef_search values tried in order, about 12 % apart above 100 so the smallest ef reaching the target is found
+# closely; the engine accepts up to 4096
+EF_LADDER = (45, 60, 80, 100, 112, 125, 140, 160, 180, 200, 225, 256, 288, 320, 360, 400, 450, 512, 576, 640, 720,
+             800, 900, 1024, 1152, 1280, 1440, 1600, 1800, 2048, 2304, 2560, 2880, 3200, 3600, 4096)
 CALIB_QUERIES = 2000
 
 
