@@ -150,7 +150,7 @@ struct Vamana {
       if (w > 0 && pool[w - 1].id == pool[i].id) continue;
       pool[w++] = pool[i];
     }
-    pool.resize(w);
+    pool.resize(std::min<size_t>(w, static_cast<size_t>(qv_vamana::kMaxOcclusion)));
     s.pruned.assign(pool.size(), 0);
     out.clear();
     for (size_t i = 0; i < pool.size() && static_cast<int32_t>(out.size()) < R; ++i) {

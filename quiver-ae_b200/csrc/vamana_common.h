@@ -3,8 +3,8 @@
 // so both insert the same points in the same batches from the same medoid.
 //
 // Construction (Subramanya et al., "DiskANN", NeurIPS 2019): greedy search
-// from the medoid with list size L, RobustPrune(p, V, alpha, R), reverse
-// edges re-pruned when a list overflows.  Points are inserted in batches in
+// from the medoid with list size L, RobustPrune(p, V, alpha, R) over at most
+// kMaxOcclusion candidates, reverse edges re-pruned when a list overflows.  Points are inserted in batches in
 // a seeded order; the searches of a batch run on the graph as it stood when
 // the batch began.  Pass 0 (of two) uses alpha = 1 and batches that double
 // from 1; later passes use the final alpha and full batches.
@@ -58,6 +58,11 @@ inline std::vector<int64_t> insertion_order(uint64_t seed, int64_t n) {
 // Batches grow to 2 % of n, at most 2^21 points (for n <= 1M that is at
 // most 20,000 points).
 inline int64_t max_batch(int64_t n) { return std::max<int64_t>(1, std::min<int64_t>(n / 50, int64_t(1) << 21)); }
+
+// RobustPrune keeps at most this many of its candidates, nearest first (after removing the point itself and
+// repeated ids), before the occlusion loop: DiskANN's candidate cap for pruning (its max_occlusion_size,
+// default 750).  Only a reverse-edge pool of a node that many new points link to in one batch reaches it.
+constexpr int32_t kMaxOcclusion = 750;
 
 inline float pass_alpha(int32_t pass, int32_t passes, float alpha_final) {
   return (passes > 1 && pass == 0) ? 1.0f : alpha_final;

@@ -22,7 +22,10 @@
 #include <cub/cub.cuh>
 
 #include <algorithm>
+#include <chrono>
 #include <cstdint>
+#include <cstdio>
+#include <cstdlib>
 #include <string>
 #include <vector>
 
@@ -163,8 +166,9 @@ __device__ bool seen_insert(unsigned long long* tab, uint32_t tag, int32_t id, i
 }
 
 // RobustPrune(p, pool, alpha, R) of index_build.cpp: sort the pool by (d, id),
-// drop p and repeats, then take the nearest remaining candidate and discard
-// every later one it covers (alpha * d(c, c') < d(p, c')).  pool_d/pool_i hold
+// drop p and repeats, keep the nearest kMaxOcclusion, then take the nearest
+// remaining candidate and discard every later one it covers
+// (alpha * d(c, c') < d(p, c')).  pool_d/pool_i hold
 // P entries; sd/si are scratch of the same size; returns the out-degree.
 template <typename T>
 __device__ int robust_prune(const VArgs& a, int64_t p, float* pd, int32_t* pi, int P, float* sd, int32_t* si,
@@ -195,6 +199,7 @@ __device__ int robust_prune(const VArgs& a, int64_t p, float* pd, int32_t* pi, i
     }
     w += __popc(m);
   }
+  w = min(w, qv_vamana::kMaxOcclusion);  // the candidate cap, nearest first
   for (int k = lane; k < (w + 31) / 32; k += 32) pruned[k] = 0u;
   __syncwarp();
   int o = 0;
@@ -404,6 +409,87 @@ __global__ void install_kernel(const VArgs a, int64_t first, int64_t cnt, unsign
                              : kNoKey;
 }
 
+// Pools above this size are cut to their kMaxOcclusion nearest by a radix
+// select before the (quadratic) rank sort of robust_prune.
+constexpr int kSelectAbove = 1024;
+
+// One warp: moves the `keep` smallest of the P keys (float bits of pd[i], pi[i])
+// -- which are distinct, as the ids of a reverse-edge pool are -- to the front of
+// pd / pi in their old order, by an 8-bit-digit radix select over the 64-bit
+// keys.  Distances are >= 0, so their float bits order like the floats.
+// hist: 256 words of this warp's shared memory.  Returns keep.
+__device__ int select_nearest(float* pd, int32_t* pi, int P, int keep, unsigned* hist, int lane) {
+  auto key = [&](int i) {
+    return (static_cast<unsigned long long>(__float_as_uint(pd[i])) << 32) | static_cast<uint32_t>(pi[i]);
+  };
+  unsigned long long prefix = 0;  // the digits of the keep-th smallest key found so far
+  int need = keep;                // its rank among the keys that share those digits
+  for (int shift = 56; shift >= 0; shift -= 8) {
+    for (int b = lane; b < 256; b += 32) hist[b] = 0u;
+    __syncwarp();
+    const unsigned long long hi = shift == 56 ? 0ull : (~0ull << (shift + 8));
+    for (int i = lane; i < P; i += 32) {
+      const unsigned long long k = key(i);
+      if ((k & hi) == prefix) atomicAdd(&hist[(k >> shift) & 255u], 1u);
+    }
+    __syncwarp();
+    unsigned c[8], sum = 0;
+#pragma unroll
+    for (int t = 0; t < 8; ++t) {
+      c[t] = hist[8 * lane + t];
+      sum += c[t];
+    }
+    unsigned incl = sum;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const unsigned v = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += v;
+    }
+    const unsigned excl = incl - sum;
+    const bool mine = excl < static_cast<unsigned>(need) && static_cast<unsigned>(need) <= incl;
+    const int src = __ffs(__ballot_sync(0xffffffffu, mine)) - 1;
+    int digit = 0;
+    unsigned before = excl;
+    if (mine) {
+      for (int t = 0; t < 8; ++t) {
+        if (before + c[t] >= static_cast<unsigned>(need)) {
+          digit = 8 * lane + t;
+          break;
+        }
+        before += c[t];
+      }
+    }
+    digit = __shfl_sync(0xffffffffu, digit, src);
+    before = __shfl_sync(0xffffffffu, before, src);
+    prefix |= static_cast<unsigned long long>(digit) << shift;
+    need -= static_cast<int>(before);
+    __syncwarp();
+  }
+  // prefix is now the keep-th smallest key itself: keep every key <= it, in order
+  int w = 0;
+  for (int base = 0; base < P; base += 32) {
+    const int i = base + lane;
+    float dv = 0.f;
+    int32_t iv = 0;
+    bool take = false;
+    if (i < P) {
+      dv = pd[i];
+      iv = pi[i];
+      take = ((static_cast<unsigned long long>(__float_as_uint(dv)) << 32) | static_cast<uint32_t>(iv)) <= prefix;
+    }
+    const unsigned m = __ballot_sync(0xffffffffu, take);
+    __syncwarp();  // every lane has read its entry before any moves down
+    if (take) {
+      const int at = w + __popc(m & ((1u << lane) - 1u));
+      pd[at] = dv;
+      pi[at] = iv;
+    }
+    w += __popc(m);
+    __syncwarp();
+  }
+  return w;
+}
+
 // ------------------------------------------------------ 4. reverse edges --
 
 struct RevArgs {
@@ -446,6 +532,7 @@ __global__ void __launch_bounds__(kWarps * 32) reverse_kernel(const VArgs a, Rev
   float* wpd = r.pd + wid * r.pool_per_warp;
   int32_t* wpi = r.pi + wid * r.pool_per_warp;
   uint32_t* pruned = r.bits + wid * r.bits_per_warp;
+  __shared__ unsigned s_hist[kWarps][256];
   for (int g = static_cast<int>(wid); g < nh; g += gridDim.x * kWarps) {
     const int64_t h = r.heads[g];
     const int32_t j = static_cast<int32_t>(r.keys[h] >> 32);
@@ -484,7 +571,7 @@ __global__ void __launch_bounds__(kWarps * 32) reverse_kernel(const VArgs a, Rev
       continue;
     }
     // overflow: re-prune old list + new p's (P <= R + longest group: the pool fits)
-    const int P = deg + nadd;
+    int P = deg + nadd;
     float* pd = wpd;
     int32_t* pi = wpi;
     const T* vj = data + static_cast<int64_t>(j) * a.dim;
@@ -511,6 +598,9 @@ __global__ void __launch_bounds__(kWarps * 32) reverse_kernel(const VArgs a, Rev
       at += __popc(m);
     }
     __syncwarp();
+    // a large pool (a node many of the batch's points link to) goes to its kMaxOcclusion nearest first:
+    // the same candidates robust_prune keeps, since the pool holds neither j nor a repeated id
+    if (P > kSelectAbove) P = select_nearest(pd, pi, P, qv_vamana::kMaxOcclusion, s_hist[wib], lane);
     // prune into the list itself: robust_prune reads only the pool, so nb can take the result
     const int o = robust_prune<T>(a, j, pd, pi, P, pd + P, pi + P, alpha, nb, pruned, lane);
     for (int t = o + lane; t < a.R; t += 32) nb[t] = -1;
@@ -597,6 +687,14 @@ int run_vamana(const T* h_data, int64_t n, int32_t dim, int32_t R, int32_t L, fl
                           static_cast<int>(smem)),
      "smem attribute");
   uint32_t tag = 1;
+  // QV_BUILD_LOG=1: one stderr line per batch with the time of its searches and of its reverse-edge phase
+  // (synchronising after each, so only for diagnosis) and the size of its largest reverse-edge group
+  const char* log_env = std::getenv("QV_BUILD_LOG");
+  const bool log = log_env && *log_env && *log_env != '0';
+  auto now_ms = [&] {
+    if (log) cudaDeviceSynchronize();
+    return std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now().time_since_epoch()).count();
+  };
   for (int32_t pass = 0; pass < passes && err.empty(); ++pass) {
     const float alpha = qv_vamana::pass_alpha(pass, passes, alpha_final);
     int64_t start = 0;
@@ -604,6 +702,7 @@ int run_vamana(const T* h_data, int64_t n, int32_t dim, int32_t R, int32_t L, fl
     while (start < n && err.empty()) {
       const int64_t end = std::min(n, start + bsize);
       const int64_t cnt = end - start;
+      const double t0 = log ? now_ms() : 0.0;
       for (int64_t c0 = 0; c0 < cnt; c0 += chunk) {
         const int ch = static_cast<int>(std::min<int64_t>(chunk, cnt - c0));
         if (tag + static_cast<uint32_t>(ch) < tag) {  // tags wrapped: clear the sets
@@ -614,6 +713,7 @@ int run_vamana(const T* h_data, int64_t n, int32_t dim, int32_t R, int32_t L, fl
                                                                                    alpha);
         tag += static_cast<uint32_t>(ch);
       }
+      const double t1 = log ? now_ms() : 0.0;
       const int64_t total = cnt * R;
       install_kernel<<<static_cast<unsigned>((total + 255) / 256), 256>>>(a, start, cnt, keys);
       ck(cub::DeviceRadixSort::SortKeys(sort_tmp, sort_bytes, keys, keys2, static_cast<int>(total)), "sort");
@@ -648,6 +748,10 @@ int run_vamana(const T* h_data, int64_t n, int32_t dim, int32_t R, int32_t L, fl
         RevArgs r{keys2, total, heads2, nheads, rpd, rpi, rbits, per_warp, bits_per_warp};
         reverse_kernel<T><<<static_cast<unsigned>(warps / kWarps), kWarps * 32>>>(a, r, alpha);
       }
+      if (log)
+        std::fprintf(stderr, "[vamana_gpu] pass %d batch at %lld: %lld points, search %.1f ms, reverse %.1f ms, "
+                     "%d groups, largest %d\n", pass, static_cast<long long>(start), static_cast<long long>(cnt),
+                     t1 - t0, now_ms() - t1, nh[0], nh[2]);
       int32_t e[2] = {0, 0};
       ck(cudaGetLastError(), "build kernel launch");  // a refused launch leaves the error words clear
       ck(cudaMemcpy(e, a.err, 8, cudaMemcpyDeviceToHost), "build kernels");

@@ -123,3 +123,31 @@ def test_gpu_pq_encode_equals_host(dtype, dim, M):
     piv, cen, offs = builder.pq_train(base, M, sample=5000, iters=4, seed=1)
     np.testing.assert_array_equal(builder.pq_encode(base, piv, cen, offs, device=0),
                                   builder.pq_encode(base, piv, cen, offs))
+
+
+@pytest.mark.gpu
+def test_gpu_graph_equals_host_graph_with_a_hub(capfd):
+    """A point that every new point links to: 60,000 unit vectors in 256 dimensions (nearly equidistant from
+    one another) and one vector at the origin, nearer to all of them.  Each batch of 1,200 points sends
+    the origin 1,200 new edges, so its reverse-edge pool (R + 1,200 > 1,024) is cut to its 750 nearest by
+    the GPU's radix select before pruning, and the near-ties of the distances test the select's order
+    (distance bits, then id) against the host's sort."""
+    import os
+    from quiver_b200 import builder
+    rng = np.random.default_rng(31)
+    x = rng.normal(size=(60000, 256))
+    x /= np.linalg.norm(x, axis=1, keepdims=True)
+    x[12345] = 0.0
+    base = np.ascontiguousarray(x.astype(np.float32))
+    g_h, d_h, m_h = builder.vamana(base, R=16, L=24, alpha=1.2, passes=2, seed=31)
+    os.environ["QV_BUILD_LOG"] = "1"
+    try:
+        g_g, d_g, m_g = builder.vamana_gpu(base, R=16, L=24, alpha=1.2, passes=2, seed=31)
+    finally:
+        del os.environ["QV_BUILD_LOG"]
+    log = capfd.readouterr().err
+    largest = [int(ln.rsplit("largest ", 1)[1]) for ln in log.splitlines() if "[vamana_gpu]" in ln]
+    assert max(largest) > 1024
+    assert m_g == m_h
+    np.testing.assert_array_equal(d_g, d_h)
+    np.testing.assert_array_equal(g_g, g_h)
