@@ -481,6 +481,43 @@ void upload_nav(qv_engine* e, const qv::NavHost& nav) {
   e->nav_start = nav.start;
 }
 
+// The page store into HBM without holding it in host memory: 64 MB pieces are
+// read into two pinned staging buffers in turn and copied while the next is
+// read, so a 41 GB store needs 128 MB of host memory, not 41 GB.
+void upload_pages_staged(qv_engine* e, const std::string& file, const std::string& backend) {
+  constexpr int64_t kChunkPages = 16384;
+  uint8_t* stage[2] = {nullptr, nullptr};
+  cudaEvent_t done[2] = {nullptr, nullptr};
+  auto release = [&] {
+    for (int b = 0; b < 2; ++b) {
+      if (done[b]) cudaEventDestroy(done[b]);
+      if (stage[b]) cudaFreeHost(stage[b]);
+    }
+  };
+  try {
+    for (int b = 0; b < 2; ++b) {
+      CK(cudaHostAlloc(reinterpret_cast<void**>(&stage[b]), kChunkPages * qv::kPage, cudaHostAllocDefault));
+      CK(cudaEventCreateWithFlags(&done[b], cudaEventDisableTiming));
+    }
+    const int64_t pages = e->L.num_pages;
+    int b = 0;
+    for (int64_t first = 0; first < pages; first += kChunkPages, b ^= 1) {
+      const int64_t n = std::min<int64_t>(kChunkPages, pages - first);
+      CK(cudaEventSynchronize(done[b]));  // the copy that last used this buffer has finished
+      qv::read_page_range(file, pages, backend, first, n, stage[b]);
+      CK(cudaMemcpyAsync(e->d_pages + first * qv::kPage, stage[b], static_cast<size_t>(n) * qv::kPage,
+                         cudaMemcpyHostToDevice, e->stream));
+      CK(cudaEventRecord(done[b], e->stream));
+    }
+    CK(cudaStreamSynchronize(e->stream));
+  } catch (...) {
+    cudaStreamSynchronize(e->stream);
+    release();
+    throw;
+  }
+  release();
+}
+
 void alloc_pages(qv_engine* e, int32_t page_store) {
   const size_t bytes = static_cast<size_t>(e->L.num_pages) * qv::kPage;
   if (page_store == QV_PAGES_HOST) {
@@ -712,6 +749,8 @@ int qv_engine_create(const qv_engine_opts* opts, qv_engine** out) {
     } else if (opts->page_store == QV_PAGES_SHARED) {
       if (opts->validate) fail(QV_ERR_INVALID_ARG, "validate needs the whole page store, not one stripe");
       load_own_stripe(e.get(), page_file, opts->num_stripes, opts->stripe_rank);
+    } else if (opts->page_store == QV_PAGES_HBM && !opts->validate) {
+      upload_pages_staged(e.get(), page_file, backend);
     } else {
       std::vector<uint8_t> host(bytes);
       qv::read_pages(page_file, e->L.num_pages, backend, host.data());

@@ -209,6 +209,36 @@ void read_pages(const std::string& path, int64_t num_pages, const std::string& b
   ::close(fd);
 }
 
+void read_page_range(const std::string& path, int64_t num_pages, const std::string& backend, int64_t first,
+                     int64_t count, uint8_t* dst) {
+  if (first < 0 || count < 0 || first + count > num_pages)
+    throw IoError(QV_ERR_INVALID_ARG, "page range outside the page store");
+  if (count == 0) return;
+  const size_t bytes = static_cast<size_t>(count) * kPage;
+  if (backend == "heap") {
+    File f(path);
+    f.seek((first + 1) * kPage, path);
+    f.read(dst, bytes, path + " (page store)");
+    return;
+  }
+  if (backend != "mmap") throw IoError(QV_ERR_INVALID_ARG, "memory backend must be heap or mmap");
+  const int fd = ::open(path.c_str(), O_RDONLY);
+  if (fd < 0) throw IoError(QV_ERR_IO, "Failed to open mmap Mem Index " + path);
+  struct stat st {};
+  if (fstat(fd, &st) != 0 || st.st_size < (num_pages + 1) * kPage) {
+    ::close(fd);
+    throw IoError(QV_ERR_BAD_INDEX, "mmap Mem Index " + path + " is too small");
+  }
+  void* m = mmap(nullptr, bytes, PROT_READ, MAP_PRIVATE, fd, static_cast<off_t>((first + 1) * kPage));
+  if (m == MAP_FAILED) {
+    ::close(fd);
+    throw IoError(QV_ERR_IO, "Failed to mmap Mem Index " + path);
+  }
+  std::memcpy(dst, m, bytes);
+  munmap(m, bytes);
+  ::close(fd);
+}
+
 void read_stripe_pages(const std::string& path, int64_t num_pages, int32_t num_stripes, int32_t rank,
                        uint8_t* dst) {
   const int fd = ::open(path.c_str(), O_RDONLY);

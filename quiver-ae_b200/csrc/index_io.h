@@ -57,6 +57,10 @@ void check_layout(const Layout& L, const PQTables* pq);
 // bytes).  backend: "heap" (fread) or "mmap" (map then copy).
 void read_pages(const std::string& path, int64_t num_pages, const std::string& backend,
                 uint8_t* dst);
+// Pages [first, first + count) of the page store (page p is file page p + 1),
+// with the same backends as read_pages; the file must hold all num_pages.
+void read_page_range(const std::string& path, int64_t num_pages, const std::string& backend, int64_t first,
+                     int64_t count, uint8_t* dst);
 // Pages rank, rank + S, rank + 2S, ... of the page file (one stripe of S),
 // gathered through a read-only mapping so only those pages are touched.
 void read_stripe_pages(const std::string& path, int64_t num_pages, int32_t num_stripes, int32_t rank,

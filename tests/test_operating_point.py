@@ -163,3 +163,19 @@ def test_config0_ef320_w1_matches_reference_kernel(config0, policy):
         np.testing.assert_array_equal(out["dists"].view(np.uint32), ref["dists"].view(np.uint32))
         np.testing.assert_array_equal(out["found"], ref["found"])
     np.testing.assert_array_equal(orc["steps"], ref["steps"])
+
+
+def test_config0_page_store_loads_agree(config0):
+    """The 410 MB page store reaches HBM in 64 MB pieces through pinned staging buffers (seven pieces here),
+    from the heap or the mmap backend, or whole through host memory when the adjacency is validated first:
+    the three engines return the same results."""
+    from quiver_b200 import Engine, SearchParams
+    p = SearchParams(topk=10, ef_search=100, pipe_width=2, early_exit_policy="none")
+    q = config0["q"][:200]
+    outs = []
+    for kw in ({}, {"memory_backend": "mmap"}, {"validate": True}):
+        with Engine.open(config0["dir"], "uint8", **kw) as eng:
+            outs.append(eng.search(q, p))
+    for o in outs[1:]:
+        for a, b in zip(o, outs[0]):
+            np.testing.assert_array_equal(a, b)
