@@ -1,16 +1,19 @@
 #!/usr/bin/env python
 """Throughput of Quiver's query hot path on B200.
 
-One step = one search pass over one batch of synthetic queries (10K rows of
-the workload's query stream) against the workload's index, top-10, at the
-smallest ef_search from a fixed ladder whose Recall@10 reaches the target
-(0.90 by default).  Prints one JSON line on rank 0.
+One step = one search pass over one batch of synthetic queries (the
+workload's step batch: 100K rows of its query stream for the default
+config 2, 100M x 128 uint8; 10K for config 0) against the workload's index,
+top-10, at the smallest ef_search from a fixed ladder whose Recall@10
+reaches the target (0.90 by default).  The index is built on the GPU at the
+start of the run and cached for later runs on the same machine.  Prints one
+JSON line on rank 0.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
 
 N > 1 runs under torchrun: each rank holds a replica of the index and
-searches its own 10K-query batch per step (weak scaling, no collective on
-the data path; the barrier and the max-over-ranks timing use NCCL).
+searches its own step batch (weak scaling, no collective on the data path;
+the barrier and the max-over-ranks timing use NCCL).
 
 Besides the headline (HBM page store), the line carries: ``latency_mode``
 (batches of 1, 4 and 16 end to end), ``host_pages`` at N = 1 (node records
@@ -212,7 +215,8 @@ def reference_arm(args, rank: int, world: int) -> int:
     ix = pyoracle.load_index(d, w.data_type)
     nav = pyoracle.load_nav(workloads.prepare_nav(w, log=log), w.data_type) if args.nav else None
     qc = workloads.queries(w, rows=CALIB_QUERIES).astype(np.float32)
-    gtc = workloads.ground_truth(w, qc, 10)
+    # ground truth, like the index, is an input: brute force on the GPU when there is one
+    gtc = workloads.ground_truth(w, qc, 10, device=None if build_dev is None else f"cuda:{build_dev}")
     search_kw = dict(topk=w.topk, pipe_width=args.pipe_width, early_exit_policy=args.early_exit, nav=nav,
                      visited_filter=args.visited_filter)
     if args.ef > 0:
@@ -421,7 +425,9 @@ def main() -> int:
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--config", default="config0")
+    ap.add_argument("--config", default="config2",
+                    help="workload (quiver_b200.workloads.CONFIGS); config2, the metric's largest single-GPU "
+                         "configuration, builds its index on the GPU first (about 5 minutes)")
     ap.add_argument("--ef", type=int, default=0, help="fixed ef_search (0: smallest ladder ef reaching the target)")
     ap.add_argument("--target-recall", type=float, default=0.90)
     ap.add_argument("--pipe-width", type=int, default=2)
