@@ -211,3 +211,23 @@ def test_exact_routing_diagnostic(u8_index):
     r_ex = pyoracle.calc_recall(ex["ids"], u8_index["gt"], 10)
     assert r_ex >= r_pq
     assert not np.array_equal(pq["ids"], ex["ids"])
+
+
+def test_recall_attribution_script_runs_on_the_host(tmp_path):
+    """tests/recall_attribution.py (the PQ-versus-exact-routing diagnosis) on a small workload, host only:
+    one JSON line per ef with both walks, exact routing at least as good as PQ routing."""
+    import json
+    import os
+    import subprocess
+    import sys
+    from pathlib import Path
+    script = Path(__file__).resolve().parent / "recall_attribution.py"
+    env = dict(os.environ, QUIVER_B200_CACHE=str(tmp_path / "cache"))
+    res = subprocess.run([sys.executable, str(script), "--config", "config0-20k", "--queries", "200", "--efs",
+                          "20,60", "--device", "-1"], capture_output=True, text=True, env=env, timeout=600)
+    assert res.returncode == 0, res.stderr[-2000:]
+    rows = [json.loads(ln) for ln in res.stdout.splitlines() if ln.startswith("{")]
+    walks = [r for r in rows if "ef_search" in r]
+    assert [r["ef_search"] for r in walks] == [20, 60]
+    for r in walks:
+        assert r["exact_routing"]["recall_at_10"] >= r["pq_routing"]["recall_at_10"]
